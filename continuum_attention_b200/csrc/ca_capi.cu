@@ -1,0 +1,180 @@
+// ca_capi.cu -- the extern "C" entry points declared in
+// include/continuum_attention_b200.h: argument validation, workspace layout
+// and dispatch between the SIMT and tcgen05 kernel families.
+//
+// Error behaviour mirrors the reference binding (TORCH_CHECK on dtype, shape
+// and contiguity, then C10_CUDA_KERNEL_LAUNCH_CHECK after each launch,
+// cuda/continuum_attention.py:460-605): every check failure returns a status
+// code and leaves a message for ca_last_error(); nothing is launched after a
+// failed check.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "ca_internal.h"
+#include "continuum_attention_b200.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_last_launches = 0;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return CA_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(CA_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+constexpr size_t kAlign = 256;
+constexpr long long kMinKeyTile = 64;  // smallest key tile of any backward kernel
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Layout {
+  size_t rowdot, dq_acc, gain_part, total;
+  int nparts;
+};
+
+Layout workspace_layout(long long B, long long H, long long T, long long D) {
+  Layout l;
+  const size_t rows = (size_t)B * H * T;
+  l.nparts = (int)((T + kMinKeyTile - 1) / kMinKeyTile);
+  l.rowdot = 0;
+  l.dq_acc = align_up(l.rowdot + rows * sizeof(float));
+  l.gain_part = align_up(l.dq_acc + rows * (size_t)D * sizeof(float));
+  l.total = align_up(l.gain_part + (size_t)B * H * l.nparts * sizeof(float));
+  return l;
+}
+
+int check_shape(long long B, long long H, long long T, long long D, int dtype, int impl) {
+  if (B < 0 || H < 0 || T < 0 || D < 0)
+    return fail(CA_ERR_INVALID_ARGUMENT, "negative shape [B,H,T,D]=[%lld,%lld,%lld,%lld]", B, H, T, D);
+  if (D == 0 && B * H * T > 0) return fail(CA_ERR_INVALID_ARGUMENT, "head dim D must be >= 1");
+  if (dtype < CA_DTYPE_F32 || dtype > CA_DTYPE_F16)
+    return fail(CA_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (impl < CA_IMPL_AUTO || impl > CA_IMPL_TCGEN05)
+    return fail(CA_ERR_INVALID_ARGUMENT, "unknown impl code %d", impl);
+  if (D > 128) return fail(CA_ERR_UNSUPPORTED, "head dim D=%lld > 128 is not supported", D);
+  if (T > (1LL << 30)) return fail(CA_ERR_UNSUPPORTED, "sequence length T=%lld too large", T);
+  const long long BH = B * H;
+  const long long tiles = BH * ((T + 63) / 64);
+  if (tiles > 0x7fffffffLL) return fail(CA_ERR_UNSUPPORTED, "B*H*ceil(T/64)=%lld exceeds the grid", tiles);
+  return CA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ca_abi_version(void) { return CA_ABI_VERSION; }
+
+const char* ca_last_error(void) { return g_last_error.c_str(); }
+
+int ca_row_stats_floats(void) { return 2; }
+
+int ca_last_launch_count(void) { return g_last_launches; }
+
+int ca_forward(const void* q, const void* k, const void* v, const float* log_gain, void* o,
+               float* o_f32, float* row_stats, int64_t B, int64_t H, int64_t T, int64_t D,
+               int dtype, int impl, void* stream) {
+  int st = check_shape(B, H, T, D, dtype, impl);
+  if (st != CA_OK) return st;
+  if (B * H * T == 0) return ok();
+  if (!q || !k || !v || !log_gain || !o || !row_stats)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_forward: null q/k/v/log_gain/o/row_stats pointer");
+  ca::FwdArgs a{q, k, v, log_gain, o, o_f32, row_stats, B, H, T, D, dtype,
+                (float)(1.0 / std::sqrt((double)D)), (cudaStream_t)stream};
+  cudaError_t e;
+  g_last_launches = 0;
+  if (impl == CA_IMPL_SIMT) {
+    e = ca::simt::forward(a);
+    g_last_launches = ca::simt::kForwardLaunches;
+  } else if (ca::sm100::forward_supported(a)) {
+    e = ca::sm100::forward(a);
+    g_last_launches = ca::sm100::forward_launches(a);
+  } else if (impl == CA_IMPL_TCGEN05) {
+    return fail(CA_ERR_UNSUPPORTED,
+                "ca_forward: tcgen05 kernels need bf16/f16, D in {64}, 16-byte aligned buffers "
+                "(got dtype=%d D=%lld)", dtype, (long long)D);
+  } else {
+    e = ca::simt::forward(a);
+    g_last_launches = ca::simt::kForwardLaunches;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ca_forward launch");
+  return ok();
+}
+
+size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, int dtype) {
+  (void)dtype;
+  if (B <= 0 || H <= 0 || T <= 0 || D <= 0) return 0;
+  return workspace_layout(B, H, T, D).total;
+}
+
+int ca_backward(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
+                float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                int64_t T, int64_t D, int dtype, int impl, void* stream) {
+  int st = check_shape(B, H, T, D, dtype, impl);
+  if (st != CA_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (B * H * T == 0) {
+    if (dlog_gain && H > 0) {
+      cudaError_t e = cudaMemsetAsync(dlog_gain, 0, (size_t)H * sizeof(float), s);
+      if (e != cudaSuccess) return cuda_fail(e, "ca_backward memset");
+    }
+    return ok();
+  }
+  if (!q || !k || !v || !o || !d_o || !log_gain || !row_stats || !dq || !dk || !dv)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: null tensor pointer");
+  const Layout l = workspace_layout(B, H, T, D);
+  if (!workspace || workspace_bytes < l.total)
+    return fail(CA_ERR_WORKSPACE, "ca_backward: workspace of %zu bytes < required %zu", workspace_bytes,
+                l.total);
+  if (((uintptr_t)workspace) % kAlign != 0)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: workspace must be %zu-byte aligned", kAlign);
+  char* ws = (char*)workspace;
+  ca::BwdWorkspace w{(float*)(ws + l.rowdot), (float*)(ws + l.dq_acc), (float*)(ws + l.gain_part),
+                     l.nparts};
+  ca::BwdArgs a{q, k, v, o, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
+                (float)(1.0 / std::sqrt((double)D)), s};
+  cudaError_t e;
+  g_last_launches = 0;
+  if (impl == CA_IMPL_SIMT) {
+    e = ca::simt::backward(a, w);
+    g_last_launches = ca::simt::backward_launches(a);
+  } else if (ca::sm100::backward_supported(a)) {
+    e = ca::sm100::backward(a, w);
+    g_last_launches = ca::sm100::backward_launches(a);
+  } else if (impl == CA_IMPL_TCGEN05) {
+    return fail(CA_ERR_UNSUPPORTED, "ca_backward: tcgen05 kernels do not cover dtype=%d D=%lld", dtype,
+                (long long)D);
+  } else {
+    e = ca::simt::backward(a, w);
+    g_last_launches = ca::simt::backward_launches(a);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ca_backward launch");
+  return ok();
+}
+
+int ca_device_status(int reset) {
+  int value = 0;
+  cudaError_t e = ca::read_device_status(&value, reset != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_device_status");
+  return value;
+}
+
+}  // extern "C"

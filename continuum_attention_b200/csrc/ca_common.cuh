@@ -1,0 +1,114 @@
+// ca_common.cuh -- element conversions and the per-segment moment math shared
+// by every Continuum Attention kernel in this library.
+//
+// Notation (one query row, scores in natural-log units, m = reference max):
+//   segment k runs from key k-1 (score a) to key k (score b), d = b - a,
+//   Ea = e^{a-m}, Eb = e^{b-m},  M_n = e^{a-m} J_n(d),  J_n(d) = int_0^1 u^n e^{d u} du.
+// Integration by parts gives the exact recurrences
+//   M_0 = (Eb - Ea)/d,   M_n = (Eb - n M_{n-1})/d,
+// which need one reciprocal per segment but cancel catastrophically as d -> 0
+// (M_n loses about n+1 digits times log10(1/|d|)).  For |d| < kSeriesMax the
+// highest moment needed comes from its power series
+//   J_n(d) = sum_k d^k / (k! (k+n+1))
+// and the lower ones from the downward form M_{n-1} = (Eb - d M_n)/n, which is
+// stable for |d| < 1.  Ten series terms leave a truncation error below
+// 1/(10! * 12) ~ 2.3e-8 relative at |d| = 1.
+// Reference: the same moments appear as seg_L/seg_mu (cuda/continuum_attention.py:95-113)
+// and moments() (:165-190); the float64 form is analytic_reference.py:12-49.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ca {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kSeriesMax = 1.0f;
+
+// 2^x on the MUFU pipe (relative error about 2^-22; flushes subnormal results to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 1/x on the MUFU pipe (at most 1 ulp error).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// e^x for x <= 0 relative to a row max (x = -inf gives 0).
+__device__ __forceinline__ float exp_rel(float x) { return ex2_approx(x * kLog2e); }
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// J_1(d) by its power series: sum_{k<10} d^k / (k! (k+2)).
+__device__ __forceinline__ float series_j1(float d) {
+  float p = 1.f / 3991680.f;
+  p = fmaf(p, d, 1.f / 403200.f);
+  p = fmaf(p, d, 1.f / 45360.f);
+  p = fmaf(p, d, 1.f / 5760.f);
+  p = fmaf(p, d, 1.f / 840.f);
+  p = fmaf(p, d, 1.f / 144.f);
+  p = fmaf(p, d, 1.f / 30.f);
+  p = fmaf(p, d, 1.f / 8.f);
+  p = fmaf(p, d, 1.f / 3.f);
+  p = fmaf(p, d, 1.f / 2.f);
+  return p;
+}
+
+// J_2(d) by its power series: sum_{k<10} d^k / (k! (k+3)).
+__device__ __forceinline__ float series_j2(float d) {
+  float p = 1.f / 4354560.f;
+  p = fmaf(p, d, 1.f / 443520.f);
+  p = fmaf(p, d, 1.f / 50400.f);
+  p = fmaf(p, d, 1.f / 6480.f);
+  p = fmaf(p, d, 1.f / 960.f);
+  p = fmaf(p, d, 1.f / 168.f);
+  p = fmaf(p, d, 1.f / 36.f);
+  p = fmaf(p, d, 1.f / 10.f);
+  p = fmaf(p, d, 1.f / 4.f);
+  p = fmaf(p, d, 1.f / 3.f);
+  return p;
+}
+
+// Forward moments of one segment: M0 = segment mass, M1 = right-endpoint share.
+__device__ __forceinline__ void seg_moments01(float Ea, float Eb, float d, float& M0, float& M1) {
+  if (fabsf(d) < kSeriesMax) {
+    M1 = Ea * series_j1(d);
+    M0 = fmaf(-d, M1, Eb);
+  } else {
+    const float r = rcp_approx(d);
+    M0 = (Eb - Ea) * r;
+    M1 = (Eb - M0) * r;
+  }
+}
+
+// Backward moments of one segment: M0, M1, M2.
+__device__ __forceinline__ void seg_moments012(float Ea, float Eb, float d, float& M0, float& M1,
+                                               float& M2) {
+  if (fabsf(d) < kSeriesMax) {
+    M2 = Ea * series_j2(d);
+    M1 = 0.5f * fmaf(-d, M2, Eb);
+    M0 = fmaf(-d, M1, Eb);
+  } else {
+    const float r = rcp_approx(d);
+    M0 = (Eb - Ea) * r;
+    M1 = (Eb - M0) * r;
+    M2 = fmaf(-2.f, M1, Eb) * r;
+  }
+}
+
+}  // namespace ca

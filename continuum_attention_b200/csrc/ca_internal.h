@@ -1,0 +1,71 @@
+// ca_internal.h -- argument bundles passed from the C ABI (ca_capi.cu) to the
+// kernel families (ca_simt.cu, ca_sm100.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ca {
+
+struct FwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* log_gain;
+  void* o;
+  float* o_f32;
+  float* row_stats;  // [B*H*T][2] = (row max m, normaliser Z relative to m)
+  long long B, H, T, D;
+  int dtype;         // enum ca_dtype
+  float inv_sqrt_d;  // float32(1/sqrt(D)), as the reference's D**-0.5 scalar
+  cudaStream_t stream;
+};
+
+struct BwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* d_o;
+  const float* log_gain;
+  const float* row_stats;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* dlog_gain;  // may be null
+  long long B, H, T, D;
+  int dtype;
+  float inv_sqrt_d;
+  cudaStream_t stream;
+};
+
+// Carved out of the caller's workspace (ca_capi.cu: workspace_layout).
+struct BwdWorkspace {
+  float* rowdot;     // [B*H*T]      D_i = dO_i . O_i
+  float* dq_acc;     // [B*H*T*D]    fp32 dQ accumulator
+  float* gain_part;  // [B*H*nparts] per-(head, key tile) partial sums of dS*s
+  int nparts;
+};
+
+namespace simt {
+constexpr int kForwardLaunches = 1;
+inline int backward_launches(const BwdArgs& a) { return a.dlog_gain ? 4 : 3; }
+cudaError_t forward(const FwdArgs& a);
+cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
+}  // namespace simt
+
+namespace sm100 {
+// true when the tcgen05 kernels cover this problem (dtype, D, alignment)
+bool forward_supported(const FwdArgs& a);
+bool backward_supported(const BwdArgs& a);
+int forward_launches(const FwdArgs& a);
+int backward_launches(const BwdArgs& a);
+cudaError_t forward(const FwdArgs& a);
+cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
+}  // namespace sm100
+
+// device status word (bounded waits record CA_ERR_DEVICE_TIMEOUT here)
+cudaError_t read_device_status(int* out, bool reset);
+
+}  // namespace ca

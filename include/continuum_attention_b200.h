@@ -1,0 +1,129 @@
+/*
+ * continuum_attention_b200.h -- C ABI of the B200 (sm_100a) Continuum
+ * Attention operator.
+ *
+ * The operator computes causal Continuum Attention over [B,H,T,D] tensors:
+ * scores s_ij = exp(log_gain[h]) * q_i.k_j / sqrt(D), keys and values
+ * linearly interpolated between adjacent positions, exact per-segment
+ * exponential moments, half-token caps on the first and the last visible key,
+ * row normalisation, y = W V.  Backward is the analytic VJP.
+ *
+ * This ABI replaces the reference's pybind torch extension and the per-tile
+ * autograd loop around it:
+ *   - ca_forward  replaces _CAExactTiled.forward (cuda/continuum_attention.py:651-694)
+ *                 together with the kernels it drives: ca_scale_scores_half_kernel
+ *                 (:81-90), ca_weights_kernel (:136-163), ca_forward_half_kernel
+ *                 (:300-328), ca_direct_output_kernel (:412-457) and the torch.bmm
+ *                 GEMMs QK^T and W V (:677-690).
+ *   - ca_backward replaces _CAExactTiled.backward (:696-766) with
+ *                 ca_backward_fused_kernel (:230-293), ca_backward_half_kernel
+ *                 (:337-405), ca_scores_backward_kernel (:192-223) and the five
+ *                 torch.bmm GEMMs plus prefix add_ accumulations (:720-764).
+ *   - the Python binding that the reference loads with load_inline (:608-620,
+ *     pybind module :35-63) becomes a ctypes binding of this library.
+ *
+ * Conventions
+ *   - All tensor arguments are device pointers owned by the caller, contiguous
+ *     row-major [B,H,T,D] for q/k/v/o/do/dq/dk/dv.  The library never
+ *     allocates device memory; scratch space is passed in by the caller.
+ *   - dtype selects the element type of q/k/v/o/do/dq/dk/dv (all the same).
+ *   - log_gain is float32 [H] on the device: scale_h = exp(log_gain[h])/sqrt(D).
+ *     The fixed-tau variant passes log(1/tau) for every head.
+ *   - stream is a cudaStream_t (NULL = legacy default stream).  All work is
+ *     enqueued on it; the calls return without synchronising.
+ *   - Return value 0 = success; otherwise a CA_ERR_* code and a message that
+ *     ca_last_error() returns (thread-local, valid until the next call on the
+ *     same thread).
+ *   - Stateless and reentrant: calls on different streams from different host
+ *     threads are safe, given disjoint output and workspace buffers.
+ */
+#ifndef CONTINUUM_ATTENTION_B200_H
+#define CONTINUUM_ATTENTION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CA_ABI_VERSION 1
+
+/* element types of q/k/v/o/do/dq/dk/dv */
+enum ca_dtype { CA_DTYPE_F32 = 0, CA_DTYPE_BF16 = 1, CA_DTYPE_F16 = 2 };
+
+/* status codes */
+enum ca_status {
+  CA_OK = 0,
+  CA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, misaligned buffer */
+  CA_ERR_UNSUPPORTED = 2,      /* shape/dtype outside what the kernels cover */
+  CA_ERR_CUDA = 3,             /* a CUDA runtime call or a launch failed */
+  CA_ERR_WORKSPACE = 4,        /* workspace smaller than ca_backward_workspace_size() */
+  CA_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait gave up (see ca_device_status) */
+};
+
+/* Kernel family used by a call (ca_forward / ca_backward 'impl' argument). */
+enum ca_impl {
+  CA_IMPL_AUTO = 0,   /* tcgen05 tensor-core kernels where they apply, else SIMT */
+  CA_IMPL_SIMT = 1,   /* CUDA-core kernels: every dtype, D <= 128, fp32 arithmetic */
+  CA_IMPL_TCGEN05 = 2 /* sm_100a tcgen05/TMEM/TMA kernels: bf16/f16, D in {32,64,128} */
+};
+
+/* Version of this ABI (CA_ABI_VERSION of the built library). */
+int ca_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ca_last_error(void);
+
+/* Number of float32 per query row in the row-statistics buffer that
+ * ca_forward writes and ca_backward reads ([B*H*T * ca_row_stats_floats()]). */
+int ca_row_stats_floats(void);
+
+/*
+ * Forward.  o = CA(q, k, v) [B,H,T,D] in dtype; row_stats receives the
+ * per-row statistics the backward needs (row max and normaliser).
+ * o_f32 (optional, may be NULL) additionally receives the float32
+ * accumulator before the final rounding to dtype (o is exactly the
+ * round-to-nearest-even of o_f32 when both are written).
+ * Replaces _CAExactTiled.forward, cuda/continuum_attention.py:651-694.
+ */
+int ca_forward(const void* q, const void* k, const void* v, const float* log_gain,
+               void* o, float* o_f32, float* row_stats,
+               int64_t B, int64_t H, int64_t T, int64_t D,
+               int dtype, int impl, void* stream);
+
+/* Bytes of scratch space ca_backward needs for this shape (>= 0). */
+size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, int dtype);
+
+/*
+ * Backward.  Given the forward's o and row_stats and the upstream gradient
+ * do, writes dq, dk, dv ([B,H,T,D], dtype) and, if dlog_gain is not NULL,
+ * d loss / d log_gain [H] in float32 (summed over the batch).
+ * workspace must hold ca_backward_workspace_size() bytes (256-byte aligned);
+ * its contents on entry are ignored.
+ * Replaces _CAExactTiled.backward, cuda/continuum_attention.py:696-766.
+ */
+int ca_backward(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                const float* log_gain, const float* row_stats,
+                void* dq, void* dk, void* dv, float* dlog_gain,
+                void* workspace, size_t workspace_bytes,
+                int64_t B, int64_t H, int64_t T, int64_t D,
+                int dtype, int impl, void* stream);
+
+/* Number of kernels the last successful ca_forward / ca_backward call on this
+ * thread enqueued (memsets excluded).  Diagnostic for launch accounting. */
+int ca_last_launch_count(void);
+
+/*
+ * Device status word of the calling thread's current device: 0 if every
+ * bounded device-side wait since the last reset completed, else a CA_ERR_*
+ * code recorded by a kernel that gave up waiting.  Synchronises the device.
+ * reset != 0 clears the word after reading it.
+ */
+int ca_device_status(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONTINUUM_ATTENTION_B200_H */
