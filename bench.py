@@ -230,11 +230,11 @@ def run_ours(args, world, rank, local):
         q, k, v, dy = sets[i % N_INPUT_SETS]
         if ev is not None:
             ev[0].record(stream)
-        o, stats, _ = ca.forward_raw(q, k, v, lg, impl=impl)
+        o, stats, o32 = ca.forward_raw(q, k, v, lg, impl=impl, want_f32=True)
         nf = _native.lib().ca_last_launch_count()
         if ev is not None:
             ev[1].record(stream)
-        ca.backward_raw(q, k, v, o, dy, lg, stats, want_dgain=True, impl=impl, workspace=ws)
+        ca.backward_raw(q, k, v, o, dy, lg, stats, want_dgain=True, impl=impl, workspace=ws, o_f32=o32)
         nb = _native.lib().ca_last_launch_count()
         if ev is not None:
             ev[2].record(stream)

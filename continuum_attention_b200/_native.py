@@ -26,7 +26,7 @@ SIGNATURES = {
     "ca_row_stats_floats": (_int, []),
     "ca_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_backward_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _int]),
-    "ca_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+    "ca_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                            _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_device_status": (_int, [_int]),
     "ca_last_launch_count": (_int, []),

@@ -76,8 +76,13 @@ def workspace_bytes(B, H, T, D, dtype) -> int:
     return int(_native.lib().ca_backward_workspace_size(B, H, T, D, _DTYPE_CODE[dtype]))
 
 
-def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="auto", workspace=None):
-    """Run the native backward; returns (dq, dk, dv, dlog_gain float32 [H] or None)."""
+def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="auto", workspace=None,
+                 o_f32=None):
+    """Run the native backward; returns (dq, dk, dv, dlog_gain float32 [H] or None).
+
+    ``o_f32`` (optional) is the forward's fp32 accumulator; it makes the row
+    terms D_i = dO_i . O_i exact to fp32 for bf16/f16 inputs.
+    """
     B, H, T, D = q.shape
     lib = _native.lib()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -86,7 +91,8 @@ def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="aut
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
-        st = lib.ca_backward(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), ctypes_ptr(o), ctypes_ptr(do),
+        st = lib.ca_backward(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), None if o is None else ctypes_ptr(o),
+                             None if o_f32 is None else ctypes_ptr(o_f32), ctypes_ptr(do),
                              ctypes_ptr(log_gain_f32), ctypes_ptr(stats), ctypes_ptr(dq), ctypes_ptr(dk),
                              ctypes_ptr(dv), None if dg is None else ctypes_ptr(dg),
                              workspace.data_ptr(), workspace.numel(), B, H, T, D,
@@ -99,15 +105,19 @@ class ContinuumAttentionFunction(torch.autograd.Function):
     """Autograd op with the reference's contract (cuda/continuum_attention.py:650-766).
 
     Saves q, k, v, the output and the per-row statistics (row max and
-    normaliser) instead of recomputing the forward in the backward.
+    normaliser) instead of recomputing the forward in the backward.  For
+    bf16/f16 inputs the saved output is the fp32 accumulator, so the backward's
+    row terms D_i = dO_i . O_i carry no output rounding.
     """
 
     @staticmethod
     def forward(ctx, q, k, v, log_gain, query_tile):
         _validate(q, k, v, log_gain)
         lg = log_gain.detach().to(device=q.device, dtype=torch.float32).contiguous()
-        o, stats, _ = forward_raw(q, k, v, lg, impl=_current_impl())
-        ctx.save_for_backward(q, k, v, o, stats, lg)
+        lowp = q.dtype != torch.float32
+        o, stats, o32 = forward_raw(q, k, v, lg, impl=_current_impl(), want_f32=lowp)
+        ctx.save_for_backward(q, k, v, o32 if lowp else o, stats, lg)
+        ctx.lowp = lowp
         ctx.gain_dtype = log_gain.dtype
         ctx.query_tile = int(query_tile)
         return o
@@ -116,10 +126,12 @@ class ContinuumAttentionFunction(torch.autograd.Function):
     def backward(ctx, grad_y):
         if torch.is_grad_enabled():
             raise RuntimeError("CA analytic kernels support first-order gradients only")
-        q, k, v, o, stats, lg = ctx.saved_tensors
+        q, k, v, o_saved, stats, lg = ctx.saved_tensors
         want_dgain = bool(ctx.needs_input_grad[3])
-        dq, dk, dv, dg = backward_raw(q, k, v, o, grad_y.to(q.dtype).contiguous(), lg, stats,
-                                      want_dgain=want_dgain, impl=_current_impl())
+        # with the fp32 accumulator saved, the dtype-rounded output is not needed
+        dq, dk, dv, dg = backward_raw(q, k, v, None if ctx.lowp else o_saved, grad_y.to(q.dtype).contiguous(),
+                                      lg, stats, want_dgain=want_dgain, impl=_current_impl(),
+                                      o_f32=o_saved if ctx.lowp else None)
         return dq, dk, dv, (dg.to(ctx.gain_dtype) if dg is not None else None), None
 
 

@@ -124,8 +124,8 @@ size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, in
   return workspace_layout(B, H, T, D).total;
 }
 
-int ca_backward(const void* q, const void* k, const void* v, const void* o, const void* d_o,
-                const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
+int ca_backward(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
                 float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
                 int64_t T, int64_t D, int dtype, int impl, void* stream) {
   int st = check_shape(B, H, T, D, dtype, impl);
@@ -138,7 +138,7 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
     }
     return ok();
   }
-  if (!q || !k || !v || !o || !d_o || !log_gain || !row_stats || !dq || !dk || !dv)
+  if (!q || !k || !v || (!o && !o_f32) || !d_o || !log_gain || !row_stats || !dq || !dk || !dv)
     return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: null tensor pointer");
   const Layout l = workspace_layout(B, H, T, D);
   if (!workspace || workspace_bytes < l.total)
@@ -149,7 +149,7 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
   char* ws = (char*)workspace;
   ca::BwdWorkspace w{(float*)(ws + l.rowdot), (float*)(ws + l.dq_acc), (float*)(ws + l.gain_part),
                      l.nparts};
-  ca::BwdArgs a{q, k, v, o, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
+  ca::BwdArgs a{q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
                 (float)(1.0 / std::sqrt((double)D)), s};
   cudaError_t e;
   g_last_launches = 0;

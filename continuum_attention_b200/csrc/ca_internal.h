@@ -27,6 +27,7 @@ struct BwdArgs {
   const void* k;
   const void* v;
   const void* o;
+  const float* o_f32;  // may be null: then D_i uses o
   const void* d_o;
   const float* log_gain;
   const float* row_stats;

@@ -481,9 +481,9 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   }
 }
 
-// D_i = dO_i . O_i  (one warp per row)
-template <typename T>
-__global__ void rowdot_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+// D_i = dO_i . O_i  (one warp per row); O in the element type TO (dtype or its fp32 accumulator)
+template <typename TO, typename T>
+__global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ dout,
                               float* __restrict__ rowdot, size_t rows, int D) {
   const size_t row = (size_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -571,8 +571,12 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
 template <typename T>
 static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
   const size_t rows = (size_t)a.B * a.H * a.T;
-  rowdot_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o,
-                                                                    w.rowdot, rows, (int)a.D);
+  if (a.o_f32)
+    rowdot_kernel<float, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o,
+                                                                              w.rowdot, rows, (int)a.D);
+  else
+    rowdot_kernel<T, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o,
+                                                                          w.rowdot, rows, (int)a.D);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(w.dq_acc, 0, rows * a.D * sizeof(float), a.stream);

@@ -99,12 +99,16 @@ size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, in
  * Backward.  Given the forward's o and row_stats and the upstream gradient
  * do, writes dq, dk, dv ([B,H,T,D], dtype) and, if dlog_gain is not NULL,
  * d loss / d log_gain [H] in float32 (summed over the batch).
+ * o_f32 (optional, may be NULL) is the forward's float32 accumulator; when
+ * given, the row terms D_i = do_i . o_i use it instead of the dtype-rounded o
+ * (which may then be NULL), keeping bf16/f16 score gradients free of the
+ * output rounding.
  * workspace must hold ca_backward_workspace_size() bytes (256-byte aligned);
  * its contents on entry are ignored.
  * Replaces _CAExactTiled.backward, cuda/continuum_attention.py:696-766.
  */
-int ca_backward(const void* q, const void* k, const void* v, const void* o, const void* d_o,
-                const float* log_gain, const float* row_stats,
+int ca_backward(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                const void* d_o, const float* log_gain, const float* row_stats,
                 void* dq, void* dk, void* dv, float* dlog_gain,
                 void* workspace, size_t workspace_bytes,
                 int64_t B, int64_t H, int64_t T, int64_t D,

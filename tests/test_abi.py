@@ -78,8 +78,8 @@ def test_argument_checks_need_no_gpu():
     st, msg = _status_and_msg(lib.ca_forward(None, None, None, None, None, None, None, 0, 2, 8, 64, 1, 0, None))
     assert st == 0 and msg == ""
     fake = ctypes.c_void_p(256)
-    st, msg = _status_and_msg(lib.ca_backward(fake, fake, fake, fake, fake, fake, fake, fake, fake, fake, None,
-                                              fake, 16, 1, 2, 8, 64, 1, 0, None))
+    st, msg = _status_and_msg(lib.ca_backward(fake, fake, fake, fake, None, fake, fake, fake, fake, fake, fake,
+                                              None, fake, 16, 1, 2, 8, 64, 1, 0, None))
     assert st == 4 and "workspace" in msg
 
 

@@ -26,8 +26,9 @@ def test_golden_small_cases_fp32(impl):
 @pytest.mark.parametrize("impl", ["simt", "auto"])
 def test_golden_small_cases_lowp(dtype, impl):
     for name, inp, _ in load_small_cases():
-        outs, used = run_op(*inp, dtype=dtype, impl=impl)
-        ref = oracle(*used[:3], inp[4], used[3])
+        q, k, v, lg, dy = inp
+        outs, used = run_op(q, k, v, lg, dy, dtype=dtype, impl=impl)
+        ref = oracle(used[0], used[1], used[2], lg, used[3])
         assert_lowp_parity(outs, ref, tag=f"{name}[{impl},{dtype}]", lowp_dtype=dtype)
 
 
