@@ -569,15 +569,50 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
 }
 
 template <typename T>
-static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
+static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
   const size_t rows = (size_t)a.B * a.H * a.T;
   if (a.o_f32)
-    rowdot_kernel<float, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o,
-                                                                              w.rowdot, rows, (int)a.D);
+    rowdot_kernel<float, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o, rowdot,
+                                                                              rows, (int)a.D);
   else
-    rowdot_kernel<T, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o,
-                                                                          w.rowdot, rows, (int)a.D);
-  cudaError_t e = cudaGetLastError();
+    rowdot_kernel<T, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o, rowdot,
+                                                                          rows, (int)a.D);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rowdot(const BwdArgs& a, float* rowdot) {
+  switch (a.dtype) {
+    case 0: return rowdot_dtype<float>(a, rowdot);
+    case 1: return rowdot_dtype<__nv_bfloat16>(a, rowdot);
+    default: return rowdot_dtype<__half>(a, rowdot);
+  }
+}
+
+template <typename T>
+static cudaError_t cast_dtype(const BwdArgs& a, const float* dq_acc) {
+  const size_t n = (size_t)a.B * a.H * a.T * a.D;
+  cast_rows_kernel<T><<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
+      dq_acc, (T*)a.dq, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc) {
+  switch (a.dtype) {
+    case 0: return cast_dtype<float>(a, dq_acc);
+    case 1: return cast_dtype<__nv_bfloat16>(a, dq_acc);
+    default: return cast_dtype<__half>(a, dq_acc);
+  }
+}
+
+cudaError_t launch_gain_reduce(const BwdArgs& a, const float* part, int nparts) {
+  gain_reduce_kernel<<<(unsigned)a.H, 256, 0, a.stream>>>(part, a.dlog_gain, (int)a.B, (int)a.H, nparts);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
+  const size_t rows = (size_t)a.B * a.H * a.T;
+  cudaError_t e = launch_rowdot(a, w.rowdot);
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(w.dq_acc, 0, rows * a.D * sizeof(float), a.stream);
   if (e != cudaSuccess) return e;
@@ -585,17 +620,9 @@ static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
   else if (a.D <= 64) e = launch_bwd<T, 64>(a, w);
   else e = launch_bwd<T, 128>(a, w);
   if (e != cudaSuccess) return e;
-  const size_t n = rows * a.D;
-  cast_rows_kernel<T><<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
-      w.dq_acc, (T*)a.dq, n);
-  e = cudaGetLastError();
+  e = launch_cast_dq(a, w.dq_acc);
   if (e != cudaSuccess) return e;
-  if (a.dlog_gain) {
-    const int nkt = (int)((a.T + BK - 1) / BK);
-    gain_reduce_kernel<<<(unsigned)a.H, 256, 0, a.stream>>>(w.gain_part, a.dlog_gain, (int)a.B,
-                                                           (int)a.H, nkt);
-    e = cudaGetLastError();
-  }
+  if (a.dlog_gain) e = launch_gain_reduce(a, w.gain_part, (int)((a.T + BK - 1) / BK));
   return e;
 }
 

@@ -384,6 +384,425 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 
 }  // namespace fwd
 
+// ---------------------------------------------------------------------------
+// Backward, one CTA per 128-key tile [j0, j0+128), looping over the query
+// tiles i0 = j0, j0+128, ... (one CTA per SM):
+//   warp 16 (one elected lane) is the producer:
+//     TMA: K' and V' (keys j0-16 .. j0+143, stationary), Q and dO tiles (2 stages)
+//     S  = Q K'^T   128x160 fp32, TMEM columns [0,160)    (key j0+x at column 16+x)
+//     dP = dO V'^T  128x160 fp32, TMEM columns [160,320)
+//     dQ  = dS K        128x64 fp32, TMEM [320,384)  (fresh per query tile)
+//     dV += P^T dO      128x64 fp32, TMEM [384,448)  (lane = key)
+//     dK += dS^T Q      128x64 fp32, TMEM [448,512)
+//   warps 0-15: thread = (query row 32*(w%4)+lane, key quarter w/4 of 32 keys).
+//     It loads its 34 S and dP values (one halo key each side), forms the 33
+//     segment moments M0..M2, the analytic VJP
+//       dS_j = (R_j + L_{j+1} + cap_j g_j) / Z,   p_j = (B_j + A_{j+1} + cap_j) / Z,
+//     with g = dP - D_i (D_i = dO_i . O_i), and writes p and scale*dS as bf16
+//     into a 128-byte-swizzled shared buffer [2 key halves][128 queries][64 keys].
+//     The same bytes are the MN-major A operand of dV / dK (M = keys) and the
+//     K-major A operand of dQ (M = queries).  dQ of the previous query tile is
+//     read from TMEM and added to the fp32 dQ accumulator with red.global.add.
+// Replaces cuda/continuum_attention.py:713-764 (recompute, dW = dY V^T, the
+// analytic score VJP kernels :192-293/:337-405, and the dV/dQ/dK GEMMs).
+namespace bwd {
+
+constexpr int BM = 128;              // query rows per tile
+constexpr int BN = 128;              // keys per CTA
+constexpr int HD = 64;
+constexpr int KH = 160;              // staged key rows: j0-16 .. j0+143
+constexpr int KOFF = 16;             // TMEM / SMEM row of key j0
+constexpr int NUM_MATH_WARPS = 16;
+constexpr int NUM_THREADS = (NUM_MATH_WARPS + 1) * 32;
+constexpr int QSTAGES = 3;
+constexpr uint32_t KV_BYTES = KH * HD * 2;      // 20 KB
+constexpr uint32_t QT_BYTES = BM * HD * 2;      // 16 KB
+constexpr uint32_t HALF_BYTES = BM * 128;       // 16 KB: 128 query rows x 64 keys bf16
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t T_S = 0, T_DP = 160, T_DQ = 320, T_DV = 384, T_DK = 448;
+
+struct __align__(1024) Smem {
+  uint8_t k[KV_BYTES];
+  uint8_t v[KV_BYTES];
+  uint8_t q[QSTAGES][QT_BYTES];
+  uint8_t dout[QSTAGES][QT_BYTES];
+  uint8_t p[2][HALF_BYTES];          // P   (bf16), [key half][query row][64 keys], swizzled
+  uint8_t ds[2][HALF_BYTES];         // scale * dS (bf16), same layout
+  uint64_t bar_kv;
+  uint64_t bar_qdo[QSTAGES];
+  uint64_t bar_s_full;
+  uint64_t bar_s_consumed;
+  uint64_t bar_p_ready;
+  uint64_t bar_mma_done;
+  uint64_t bar_drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float red[NUM_MATH_WARPS];
+};
+
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+template <bool kBF16>
+__device__ __forceinline__ void issue_s_dp(const Smem& sm, int st, uint32_t tmem, uint32_t idesc) {
+  const uint32_t qa = smem_u32(sm.q[st]), oa = smem_u32(sm.dout[st]);
+  const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    mma_ss(tmem + T_S, sdesc_sw128(qa + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 32, 16, 1024), idesc,
+           kk > 0 ? 1u : 0u);
+  }
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    mma_ss(tmem + T_DP, sdesc_sw128(oa + kk * 32, 16, 1024), sdesc_sw128(va + kk * 32, 16, 1024), idesc,
+           kk > 0 ? 1u : 0u);
+  }
+}
+
+template <bool kBF16>
+__device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tmem, bool first, uint32_t id_mn,
+                                            uint32_t id_dq) {
+  const uint32_t pa = smem_u32(sm.p[0]), da = smem_u32(sm.ds[0]);
+  const uint32_t qa = smem_u32(sm.q[st]), oa = smem_u32(sm.dout[st]);
+  const uint32_t ka = smem_u32(sm.k) + KOFF * 128;
+#pragma unroll
+  for (int kk = 0; kk < BM / 16; ++kk) {   // K = query rows, 16 per step
+    const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+    // dV += P^T dO : A = P (MN-major, M = keys), B = dO (MN-major, N = d)
+    mma_ss(tmem + T_DV, sdesc_sw128(pa + kk * 2048, HALF_BYTES, 1024), sdesc_sw128(oa + kk * 2048, 16384, 1024),
+           id_mn, acc);
+    // dK += dS^T Q
+    mma_ss(tmem + T_DK, sdesc_sw128(da + kk * 2048, HALF_BYTES, 1024), sdesc_sw128(qa + kk * 2048, 16384, 1024),
+           id_mn, acc);
+  }
+#pragma unroll
+  for (int kk = 0; kk < BN / 16; ++kk) {   // K = keys, 16 per step
+    // dQ = dS K : A = dS (K-major, M = queries), B = K rows j0.. (MN-major, N = d)
+    const uint32_t a_addr = da + (kk / 4) * HALF_BYTES + (kk % 4) * 32;
+    mma_ss(tmem + T_DQ, sdesc_sw128(a_addr, 16, 1024), sdesc_sw128(ka + kk * 2048, 16384, 1024), id_dq,
+           kk > 0 ? 1u : 0u);
+  }
+}
+
+template <bool kBF16>
+__device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
+                         const CUtensorMap* tdo, int bh, int j0, int n_tiles, uint32_t tmem) {
+  volatile int* ab = &sm.abort_flag;
+  const uint32_t id_s = make_idesc(BM, KH, kBF16, false, false);
+  const uint32_t id_mn = make_idesc(BN, HD, kBF16, true, true);
+  const uint32_t id_dq = make_idesc(BM, HD, kBF16, true, false);
+  bool kv_pending = true;
+  bool q_pending[QSTAGES] = {false, false, false};
+  uint32_t q_phase[QSTAGES] = {0, 0, 0};
+
+  mbar_arrive_expect_tx(&sm.bar_kv, 2 * KV_BYTES);
+  tma_load_3d(sm.k, tk, &sm.bar_kv, 0, j0 - KOFF, bh);
+  tma_load_3d(sm.v, tv, &sm.bar_kv, 0, j0 - KOFF, bh);
+  for (int t = 0; t < QSTAGES && t < n_tiles; ++t) {
+    mbar_arrive_expect_tx(&sm.bar_qdo[t], 2 * QT_BYTES);
+    tma_load_3d(sm.q[t], tq, &sm.bar_qdo[t], 0, j0 + t * BM, bh);
+    tma_load_3d(sm.dout[t], tdo, &sm.bar_qdo[t], 0, j0 + t * BM, bh);
+    q_pending[t] = true;
+  }
+  if (mbar_wait(&sm.bar_kv, 0, ab) && mbar_wait(&sm.bar_qdo[0], 0, ab)) {
+    kv_pending = false;
+    q_pending[0] = false;
+    q_phase[0] ^= 1;
+    tc_fence_after();
+    issue_s_dp<kBF16>(sm, 0, tmem, id_s);
+    mma_commit(&sm.bar_s_full);
+    for (int t = 0; t < n_tiles; ++t) {
+      const int st = t % QSTAGES;
+      if (!mbar_wait(&sm.bar_s_consumed, t & 1, ab)) break;
+      if (t + 1 < n_tiles) {
+        const int st1 = (t + 1) % QSTAGES;
+        if (!mbar_wait(&sm.bar_qdo[st1], q_phase[st1], ab)) break;
+        q_pending[st1] = false;
+        q_phase[st1] ^= 1;
+        tc_fence_after();
+        issue_s_dp<kBF16>(sm, st1, tmem, id_s);
+        mma_commit(&sm.bar_s_full);
+      }
+      if (!mbar_wait(&sm.bar_p_ready, t & 1, ab)) break;
+      tc_fence_after();
+      issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
+      mma_commit(&sm.bar_mma_done);
+      if (t + QSTAGES < n_tiles) {
+        if (!mbar_wait(&sm.bar_mma_done, t & 1, ab)) break;
+        const int tt = t + QSTAGES;
+        mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
+        tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
+        tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
+        q_pending[st] = true;
+      }
+    }
+  }
+  // drain: every copy lands and every MMA completes before shared memory / TMEM go away
+  mma_commit(&sm.bar_drain);
+  int dummy = 0;
+  volatile int* nab = &dummy;
+  if (kv_pending) mbar_wait(&sm.bar_kv, 0, nab);
+  for (int s2 = 0; s2 < QSTAGES; ++s2)
+    if (q_pending[s2]) mbar_wait(&sm.bar_qdo[s2], q_phase[s2], nab);
+  mbar_wait(&sm.bar_drain, 0, nab);
+}
+
+template <bool kBF16>
+__device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
+                           float* dq_acc, void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
+                           int kt, int nkt, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
+  volatile int* ab = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rq = warp & 3;                 // TMEM lane quarter
+  const int qk = warp >> 2;                // key quarter: keys j0+32qk .. +31
+  const int r = rq * 32 + lane;            // query row in tile / key row in epilogue
+  const uint32_t lane_base = (uint32_t)(rq * 32) << 16;
+  const float scale = expf(log_gain[h]) * inv_sqrt_d;
+  const uint32_t colS = tmem + lane_base + T_S + KOFF + 32 * qk;    // key j0+32qk
+  const uint32_t colP = tmem + lane_base + T_DP + KOFF + 32 * qk;
+  uint8_t* const pbuf = sm.p[qk >> 1];
+  uint8_t* const dbuf = sm.ds[qk >> 1];
+  const int chunk0 = 4 * (qk & 1);         // first 16-byte chunk of this quarter in a 128-byte row
+  float gsum = 0.f;
+  bool ok = true;
+
+  for (int t = 0; t < n_tiles; ++t) {
+    const int i0 = j0 + t * BM;
+    const int i = i0 + r;
+    const bool row_ok = i < Tn;
+    float m = 0.f, iz = 0.f, dd = 0.f;
+    if (row_ok) {
+      const size_t ri = (size_t)bh * Tn + i;
+      m = stats[2 * ri];
+      iz = 1.f / stats[2 * ri + 1];
+      dd = rowdot[ri];
+    }
+    const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
+    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+    tc_fence_after();
+    uint32_t s_lo, s_hi, p_lo, p_hi;
+    uint32_t sv[2][16], pv[2][16];
+    tmem_ld1(colS - 1, s_lo);
+    tmem_ld16(colS, sv[0]);
+    tmem_ld16(colS + 16, sv[1]);
+    tmem_ld1(colS + 32, s_hi);
+    tmem_ld1(colP - 1, p_lo);
+    tmem_ld16(colP, pv[0]);
+    tmem_ld16(colP + 16, pv[1]);
+    tmem_ld1(colP + 32, p_hi);
+    tmem_ld_wait();
+    tc_fence_before();
+    mbar_arrive(&sm.bar_s_consumed);
+
+    const int kbase = j0 + 32 * qk;              // key of local column 0
+    const float m2 = m * kLog2e;
+    auto vis = [&](int key) { return row_ok && key >= 0 && key <= i; };
+    auto E = [&](float s, int key) { return vis(key) ? ex2_approx(fmaf(s, kLog2e, -m2)) : 0.f; };
+    // left halo key kbase-1 and the segment into key kbase
+    float sa = __uint_as_float(s_lo) * scale;
+    float ea = E(sa, kbase - 1);
+    float ga = __uint_as_float(p_lo) - dd;
+    float Rprev = 0.f, Bprev = 0.f;
+    float sc = __uint_as_float(sv[0][0]) * scale;
+    float ec = E(sc, kbase);
+    float gc = __uint_as_float(pv[0][0]) - dd;
+    if (vis(kbase) && kbase >= 1) {
+      float M0, M1, M2;
+      seg_moments012(ea, ec, sc - sa, M0, M1, M2);
+      const float G = gc - ga;
+      Rprev = fmaf(ga, M1, G * M2);
+      Bprev = M1;
+    }
+    if (t > 0) {
+      const bool got2 = mbar_wait(&sm.bar_mma_done, (t - 1) & 1, ab);
+      if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
+    }
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+      uint32_t pk[8], dk[8];
+#pragma unroll
+      for (int x = 0; x < 16; x += 2) {
+        float po[2], dso[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = 16 * ch + x + u;          // current key kbase + c
+          const int key = kbase + c;
+          // next key (c+1): from the register tile or the right halo
+          uint32_t sn_bits, pn_bits;
+          if (c + 1 < 32) {
+            sn_bits = sv[(c + 1) >> 4][(c + 1) & 15];
+            pn_bits = pv[(c + 1) >> 4][(c + 1) & 15];
+          } else {
+            sn_bits = s_hi;
+            pn_bits = p_hi;
+          }
+          const float sn = __uint_as_float(sn_bits) * scale;
+          const float en = E(sn, key + 1);
+          const float gn = __uint_as_float(pn_bits) - dd;
+          float Lnext = 0.f, Anext = 0.f, Rn = 0.f, Bn = 0.f;
+          if (vis(key + 1)) {
+            float M0, M1, M2;
+            seg_moments012(ec, en, sn - sc, M0, M1, M2);
+            const float G = gn - gc;
+            Anext = M0 - M1;
+            Lnext = fmaf(gc, Anext, G * (M1 - M2));
+            Rn = fmaf(gc, M1, G * M2);
+            Bn = M1;
+          }
+          float ds = 0.f, p = 0.f;
+          if (vis(key)) {
+            const float cap = 0.5f * ec * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
+            ds = (Rprev + Lnext + cap * gc) * iz;
+            p = (Bprev + Anext + cap) * iz;
+            gsum = fmaf(ds, sc, gsum);
+          }
+          po[u] = p;
+          dso[u] = ds * scale;
+          Rprev = Rn;
+          Bprev = Bn;
+          sc = sn;
+          ec = en;
+          gc = gn;
+        }
+        pk[x / 2] = kBF16 ? pack_bf16x2(po[0], po[1]) : pack_f16x2(po[0], po[1]);
+        dk[x / 2] = kBF16 ? pack_bf16x2(dso[0], dso[1]) : pack_f16x2(dso[0], dso[1]);
+      }
+      // two 16-byte chunks of this row (8 keys each), 128-byte swizzle: chunk ^ (row & 7)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int chunk = chunk0 + 2 * ch + hh;
+        const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) * 16);
+        *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
+        *reinterpret_cast<uint4*>(dbuf + off) = make_uint4(dk[4 * hh], dk[4 * hh + 1], dk[4 * hh + 2], dk[4 * hh + 3]);
+      }
+    }
+    // dQ of the previous query tile: TMEM -> fp32 accumulator in global memory
+    if (t > 0) {
+      uint32_t qv[16];
+      tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
+      tmem_ld_wait();
+      const int ip = i0 - BM + r;
+      if (ip < Tn) {
+        float* dst = dq_acc + ((size_t)bh * Tn + ip) * HD + 16 * qk;
+#pragma unroll
+        for (int x = 0; x < 16; x += 4)
+          red_add_v4(dst + x, __uint_as_float(qv[x]), __uint_as_float(qv[x + 1]), __uint_as_float(qv[x + 2]),
+                     __uint_as_float(qv[x + 3]));
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(&sm.bar_p_ready);
+  }
+
+  // last dQ tile and the dK / dV accumulators
+  if (ok) ok = mbar_wait(&sm.bar_mma_done, (n_tiles - 1) & 1, ab);
+  ok = __all_sync(0xffffffffu, ok);
+  tc_fence_after();
+  {
+    uint32_t qv[16];
+    tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
+    tmem_ld_wait();
+    const int ip = j0 + (n_tiles - 1) * BM + r;
+    if (ok && ip < Tn) {
+      float* dst = dq_acc + ((size_t)bh * Tn + ip) * HD + 16 * qk;
+#pragma unroll
+      for (int x = 0; x < 16; x += 4)
+        red_add_v4(dst + x, __uint_as_float(qv[x]), __uint_as_float(qv[x + 1]), __uint_as_float(qv[x + 2]),
+                   __uint_as_float(qv[x + 3]));
+    }
+  }
+  {
+    // warps with qk 0/1 store dV columns 32qk..32qk+31, qk 2/3 store dK columns 32(qk-2)..
+    const bool is_k = qk >= 2;
+    const int c0 = 32 * (qk & 1);
+    uint32_t av[32];
+    tmem_ld32(tmem + lane_base + (is_k ? T_DK : T_DV) + c0, av);
+    tmem_ld_wait();
+    const int key = j0 + r;
+    if (ok && key < Tn) {
+      uint16_t* base = reinterpret_cast<uint16_t*>(is_k ? dkp : dvp) + ((size_t)bh * Tn + key) * HD + c0;
+      uint4* dst = reinterpret_cast<uint4*>(base);
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float a0 = __uint_as_float(av[8 * x + 2 * u]), a1 = __uint_as_float(av[8 * x + 2 * u + 1]);
+          w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+        }
+        dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  // d log_gain partial of this key tile: sum over the CTA of dS * s
+  for (int off = 16; off > 0; off >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, off);
+  if (lane == 0) sm.red[warp] = gsum;
+  named_bar_sync(1, NUM_MATH_WARPS * 32);
+  if (gain_part && threadIdx.x == 0) {
+    float tsum = 0.f;
+    for (int w = 0; w < NUM_MATH_WARPS; ++w) tsum += sm.red[w];
+    gain_part[(size_t)bh * nkt + kt] = tsum;
+  }
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+           const float* __restrict__ log_gain, const float* __restrict__ stats, const float* __restrict__ rowdot,
+           float* __restrict__ dq_acc, void* __restrict__ dkp, void* __restrict__ dvp,
+           float* __restrict__ gain_part, int BH, int H, int Tn, float inv_sqrt_d) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = (Tn + BN - 1) / BN;
+  const int bh = blockIdx.x % BH;
+  const int kt = blockIdx.x / BH;           // low key tiles see the most query tiles: launch first
+  const int j0 = kt * BN;
+  const int n_tiles = nkt - kt;             // query tiles j0, j0+128, ...
+
+  if (warp == NUM_MATH_WARPS) {
+    if (lane == 0) {
+      mbar_init(&sm.bar_kv, 1);
+      for (int s = 0; s < QSTAGES; ++s) mbar_init(&sm.bar_qdo[s], 1);
+      mbar_init(&sm.bar_s_full, 1);
+      mbar_init(&sm.bar_s_consumed, NUM_MATH_WARPS * 32);
+      mbar_init(&sm.bar_p_ready, NUM_MATH_WARPS * 32);
+      mbar_init(&sm.bar_mma_done, 1);
+      mbar_init(&sm.bar_drain, 1);
+      sm.abort_flag = 0;
+      fence_mbar_init();
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+    }
+    __syncwarp();
+    tmem_alloc(&sm.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == NUM_MATH_WARPS) {
+    if (lane == 0) producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, bh, j0, n_tiles, tmem);
+    __syncwarp();
+  } else {
+    math_warps<kBF16>(sm, log_gain, stats, rowdot, dq_acc, dkp, dvp, gain_part, bh, bh % H, Tn, j0, kt, nkt,
+                      n_tiles, tmem, inv_sqrt_d);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == NUM_MATH_WARPS) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace bwd
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -402,13 +821,14 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [BH, T, D] 16-bit tensor, box = {64 (D), 128 (rows), 1}, 128-byte swizzle, OOB -> 0
-static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T, long long D, bool bf16) {
+// [BH, T, D] 16-bit tensor, box = {64 (D), box_rows, 1}, 128-byte swizzle, OOB -> 0
+static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T, long long D, bool bf16,
+                     unsigned box_rows = 128) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(T * D * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -423,9 +843,12 @@ bool forward_supported(const FwdArgs& a) {
   return (a.dtype == 1 || a.dtype == 2) && a.D == 64 && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
          aligned16(a.o) && (!a.o_f32 || aligned16(a.o_f32)) && encode_fn() != nullptr;
 }
-bool backward_supported(const BwdArgs&) { return false; }
+bool backward_supported(const BwdArgs& a) {
+  return (a.dtype == 1 || a.dtype == 2) && a.D == 64 && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
+         aligned16(a.d_o) && aligned16(a.dk) && aligned16(a.dv) && encode_fn() != nullptr;
+}
 int forward_launches(const FwdArgs&) { return 1; }
-int backward_launches(const BwdArgs&) { return 0; }
+int backward_launches(const BwdArgs& a) { return a.dlog_gain ? 4 : 3; }
 
 template <bool kBF16>
 static cudaError_t launch_fwd(const FwdArgs& a) {
@@ -444,7 +867,36 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
 }
 
 cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a) : launch_fwd<false>(a); }
-cudaError_t backward(const BwdArgs&, const BwdWorkspace&) { return cudaErrorNotSupported; }
+
+template <bool kBF16>
+static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
+  const long long BH = a.B * a.H;
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM) ||
+      !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH))
+    return cudaErrorInvalidValue;
+  cudaError_t e = simt::launch_rowdot(a, w.rowdot);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(w.dq_acc, 0, (size_t)BH * a.T * a.D * sizeof(float), a.stream);
+  if (e != cudaSuccess) return e;
+  auto kern = bwd::bwd_kernel<kBF16>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;
+  kern<<<dim3((unsigned)(BH * nkt)), bwd::NUM_THREADS, bwd::kSmemBytes, a.stream>>>(
+      mq, mk, mv, mdo, a.log_gain, a.row_stats, w.rowdot, w.dq_acc, a.dk, a.dv,
+      a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = simt::launch_cast_dq(a, w.dq_acc);
+  if (e != cudaSuccess) return e;
+  if (a.dlog_gain) e = simt::launch_gain_reduce(a, w.gain_part, (int)nkt);
+  return e;
+}
+
+cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w) {
+  return a.dtype == 1 ? launch_bwd<true>(a, w) : launch_bwd<false>(a, w);
+}
 
 }  // namespace sm100
 
