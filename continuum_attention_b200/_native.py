@@ -28,6 +28,8 @@ SIGNATURES = {
     "ca_backward_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _int]),
     "ca_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                            _i64, _i64, _i64, _i64, _int, _int, _vp]),
+    "ca_backward_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                   _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_device_status": (_int, [_int]),
     "ca_last_launch_count": (_int, []),
 }

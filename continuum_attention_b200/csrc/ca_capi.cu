@@ -178,3 +178,85 @@ int ca_device_status(int reset) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// ca_backward_noalloc: the backward pass for callers that cannot allocate
+// device memory.
+//
+// ca_backward needs scratch space (the per-row terms D_i, the fp32 dQ
+// accumulator and the per-tile gain partial sums) and expects the caller to
+// pass it in.  Some callers have no way to provide it: host code that reaches
+// this library only through the C interface while another component owns every
+// device allocation (for example a framework's caching allocator the caller
+// cannot call), or a service that fixes its device memory when it starts and
+// must not call cudaMalloc later (cudaMalloc can synchronise the device and
+// fails once the budget is spent).  For them the scratch lives in one fixed
+// array inside this library instead.
+//
+// Limits and behaviour:
+//   - the array holds kNoAllocScratchBytes (32 MiB); every GPU that loads this
+//     library keeps it until the process exits;
+//   - a problem whose scratch need (ca_backward_workspace_size) exceeds it is
+//     rejected with CA_ERR_UNSUPPORTED and a message naming both sizes;
+//   - the first call on a device looks up the array's device address there
+//     (cudaGetSymbolAddress) and caches it, so make that first call before any
+//     stream capture on that device;
+//   - all calls on a device share the one array and leave their contents in
+//     it; the backward clears what must start at zero (the dQ accumulator)
+//     itself, but two calls whose work overlaps on the GPU (different streams
+//     with no ordering between them) race on the array and give wrong results;
+//   - nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+int noalloc_scratch_here(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_backward_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(CA_ERR_UNSUPPORTED, "ca_backward_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "ca_backward_noalloc: cudaGetSymbolAddress of the scratch array");
+    if (!p) return fail(CA_ERR_CUDA, "ca_backward_noalloc: scratch array has no device address");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CA_OK;
+}
+
+}  // namespace
+
+extern "C" int ca_backward_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                   const float* o_f32, const void* d_o, const float* log_gain,
+                                   const float* row_stats, void* dq, void* dk, void* dv, float* dlog_gain,
+                                   int64_t B, int64_t H, int64_t T, int64_t D, int dtype, int impl,
+                                   void* stream) {
+  int st = check_shape(B, H, T, D, dtype, impl);
+  if (st != CA_OK) return st;
+  const size_t need = ca_backward_workspace_size(B, H, T, D, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(CA_ERR_UNSUPPORTED,
+                "ca_backward_noalloc: [B,H,T,D]=[%lld,%lld,%lld,%lld] needs %zu bytes of scratch, more than "
+                "the library's fixed %zu-byte array; call ca_backward with a workspace instead",
+                (long long)B, (long long)H, (long long)T, (long long)D, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    st = noalloc_scratch_here(&scratch);
+    if (st != CA_OK) return st;
+  }
+  return ca_backward(q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, scratch,
+                     kNoAllocScratchBytes, B, H, T, D, dtype, impl, stream);
+}

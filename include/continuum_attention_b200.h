@@ -114,6 +114,27 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
                 int64_t B, int64_t H, int64_t T, int64_t D,
                 int dtype, int impl, void* stream);
 
+/*
+ * Backward without caller-provided scratch.  No counterpart in the reference
+ * (its backward allocates through torch inside the extension).
+ * Same arguments and results as ca_backward minus the workspace.  It is meant
+ * for callers that cannot allocate device memory: code that reaches this
+ * library only through the C interface while something else owns all device
+ * allocations, or a service whose device memory is fixed at start-up and must
+ * not call cudaMalloc afterwards.  The scratch is a fixed 32 MiB array inside
+ * the library (held on every GPU that loads it until the process exits);
+ * problems whose ca_backward_workspace_size() exceeds it return
+ * CA_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
+ * address, so make it before any stream capture on that device.  All calls on
+ * a device share the array: calls whose GPU work overlaps (unordered streams)
+ * race and produce wrong results.  It allocates nothing.
+ */
+int ca_backward_noalloc(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                        const void* d_o, const float* log_gain, const float* row_stats,
+                        void* dq, void* dk, void* dv, float* dlog_gain,
+                        int64_t B, int64_t H, int64_t T, int64_t D,
+                        int dtype, int impl, void* stream);
+
 /* Number of kernels the last successful ca_forward / ca_backward call on this
  * thread enqueued (memsets excluded).  Diagnostic for launch accounting. */
 int ca_last_launch_count(void);
