@@ -16,6 +16,11 @@ Metric: CA fwd+bwd TFLOP/s counting the two GEMMs per direction,
 metric through the public autograd op with pinned host inputs copied in and
 gradients copied out inside the timed region.
 
+The line also carries "decoder": the CA-S decoder training step (BASELINE
+config 4, 101,205,120 parameters, 8 x 2048 random bytes per GPU, bf16 autocast,
+AdamW) in tokens/s over all ranks, with DDP over NCCL when N > 1
+(``--no-decoder`` skips it).
+
 ``--impl reference`` times the reference algorithm's CPU path (the float32
 restatement in oracle/, all host threads) on a bounded sample of the same
 workload and prints the same line with "impl": "reference".
@@ -214,6 +219,46 @@ def _make_sets(n, device, dtype, seed):
     return sets
 
 
+def run_decoder(args, world, rank, local, steps: int, warmup: int):
+    """CA-S decoder training step: 101,205,120 parameters, 8
+    sequences x 2048 random bytes per GPU, bf16 autocast, AdamW, gradient clip 1.0,
+    DDP over NCCL when world > 1 (weak scaling).  Returns a dict for the JSON line."""
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    from continuum_attention_b200.decoder import ContinuumDecoderConfig, ContinuumDecoderLM, count_parameters
+    from continuum_attention_b200.distributed import build_adamw, train_step
+    dev = torch.device("cuda", local)
+    torch.manual_seed(1337)                      # identical initial weights on every rank
+    cfg = ContinuumDecoderConfig()
+    model = ContinuumDecoderLM(cfg).to(dev)
+    nparams = count_parameters(model)["total"]
+    net = DDP(model, device_ids=[local], gradient_as_bucket_view=True) if world > 1 else model
+    opt = build_adamw(net)
+    per_gpu_batch, T = 8, cfg.block_size
+    g = torch.Generator(device="cpu").manual_seed(2000 + rank)
+    batches = [torch.randint(0, 256, (per_gpu_batch, T), generator=g).to(dev) for _ in range(4)]
+    for i in range(warmup):
+        train_step(net, opt, batches[i % 4])
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    loss = None
+    for i in range(steps):
+        loss = train_step(net, opt, batches[i % 4])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(world, e0.elapsed_time(e1))
+    tokens = world * per_gpu_batch * T * steps
+    del net, opt, model
+    torch.cuda.empty_cache()
+    return {"metric": "CA-S decoder train tokens/s (BASELINE config 4)", "value": tokens / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms / steps, "params": nparams, "per_gpu_batch": per_gpu_batch, "seq_len": T,
+            "parallelism": f"ddp{world}" if world > 1 else "single", "dtype": "bf16 autocast, fp32 master",
+            "optimizer": "AdamW(lr 3e-4, wd 0.1, betas 0.9/0.95), clip 1.0", "scaling": "weak",
+            "final_loss": float(loss.item()) if loss is not None else None, "data": "synthetic uniform bytes"}
+
+
 def run_ours(args, world, rank, local):
     import continuum_attention_b200 as ca
     from continuum_attention_b200 import _native
@@ -320,6 +365,9 @@ def run_ours(args, world, rank, local):
         cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
     clocks = clk.summary()
+    decoder = None
+    if not args.no_decoder:
+        decoder = run_decoder(args, world, rank, local, steps=args.decoder_steps, warmup=3)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -338,6 +386,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": launches,
+            "decoder": decoder,
         }
         print(json.dumps(line), flush=True)
 
@@ -350,6 +399,8 @@ def main():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--kernels", choices=["auto", "simt", "tcgen05"], default="auto")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-decoder", action="store_true", help="skip the CA-S decoder tokens/s measurement")
+    p.add_argument("--decoder-steps", type=int, default=10)
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -1,0 +1,172 @@
+"""CA-S byte decoder: the training workload that consumes the operator.
+
+Mirrors ``ContinuumDecoderConfig`` / ``ContinuumDecoderLM``
+(cuda/continuum_attention.py:784-922): a pre-norm decoder-only byte
+Transformer whose only non-standard part is Continuum Attention with a learned
+per-head score gain.  Defaults give the reference's 101,205,120 parameters
+(d_model 1024, 16 heads x 64, 8 layers, 4096-wide tanh-GELU MLP, byte vocab 256,
+untied embedding and head, RMSNorm, RoPE theta 1e4, residual projections
+initialised with std 0.02/sqrt(2 n_layers)).
+
+``attention_fn`` defaults to the CUDA operator; tests on machines without a GPU
+pass a CPU stand-in with the same signature.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .attention import continuum_attention
+
+
+@dataclass
+class ContinuumDecoderConfig:
+    """Configuration of the CA-S decoder (cuda/continuum_attention.py:784-813)."""
+    vocab_size: int = 256
+    block_size: int = 2048
+    d_model: int = 1024
+    n_heads: int = 16
+    n_layers: int = 8
+    mlp_ratio: float = 4.0
+    dropout: float = 0.0
+    eps: float = 1e-6
+    rope_theta: float = 10000.0
+    grad_checkpointing: bool = False
+    ca_query_tile: int = 64
+
+    def __post_init__(self):
+        if self.d_model % self.n_heads:
+            raise ValueError("d_model must be divisible by n_heads")
+        if (self.d_model // self.n_heads) % 2:
+            raise ValueError("RoPE needs even head dimension")
+        if self.n_layers <= 0 or self.block_size < 2 or self.ca_query_tile <= 0:
+            raise ValueError("Invalid layer, context or CA query tile count")
+        if self.dropout != 0:
+            raise ValueError("The CA operator has no attention dropout; use --dropout 0.0")
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x):
+        return self.weight * x * torch.rsqrt(x.square().mean(-1, keepdim=True) + self.eps)
+
+
+def rope_tables(T: int, D: int, theta: float, device, dtype):
+    """cos/sin tables [1,1,T,D] with each frequency repeated for its (even, odd) pair."""
+    freq = 1.0 / (theta ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+    phase = torch.outer(torch.arange(T, device=device, dtype=torch.float32), freq)
+    cos = torch.repeat_interleave(phase.cos(), 2, -1).to(dtype)[None, None]
+    sin = torch.repeat_interleave(phase.sin(), 2, -1).to(dtype)[None, None]
+    return cos, sin
+
+
+def apply_rope(q, k, theta: float):
+    """Rotary embedding on interleaved (even, odd) pairs (cuda/continuum_attention.py:825-835)."""
+    cos, sin = rope_tables(q.shape[-2], q.shape[-1], theta, q.device, q.dtype)
+
+    def rotate(t):
+        return torch.stack((-t[..., 1::2], t[..., 0::2]), -1).flatten(-2)
+
+    return q * cos + rotate(q) * sin, k * cos + rotate(k) * sin
+
+
+class ContinuumSelfAttention(nn.Module):
+    def __init__(self, dim: int, heads: int, rope_theta: float, ca_query_tile: int,
+                 attention_fn: Optional[Callable] = None):
+        super().__init__()
+        self.heads = heads
+        self.head_dim = dim // heads
+        self.rope_theta = rope_theta
+        self.ca_query_tile = ca_query_tile
+        self.qkv = nn.Linear(dim, 3 * dim, bias=False)
+        self.out = nn.Linear(dim, dim, bias=False)
+        self.out._residual_proj = True
+        # variant S: positive trainable per-head score gain g = exp(rho), starting at 1
+        self.log_qk_gain = nn.Parameter(torch.zeros(heads))
+        self.attention_fn = attention_fn or continuum_attention
+
+    def forward(self, x):
+        B, T, C = x.shape
+        qkv = self.qkv(x).reshape(B, T, 3, self.heads, self.head_dim).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv.unbind(0)
+        q, k = apply_rope(q, k, self.rope_theta)
+        y = self.attention_fn(q, k, v, self.log_qk_gain, self.ca_query_tile)
+        return self.out(y.transpose(1, 2).contiguous().reshape(B, T, C))
+
+
+class GELUMLP(nn.Module):
+    def __init__(self, dim: int, ratio: float):
+        super().__init__()
+        hidden = int(dim * ratio)
+        self.fc1 = nn.Linear(dim, hidden, bias=False)
+        self.fc2 = nn.Linear(hidden, dim, bias=False)
+        self.fc2._residual_proj = True
+
+    def forward(self, x):
+        return self.fc2(F.gelu(self.fc1(x), approximate="tanh"))
+
+
+class CADecoderBlock(nn.Module):
+    def __init__(self, cfg: ContinuumDecoderConfig, attention_fn=None):
+        super().__init__()
+        d = cfg.d_model
+        self.norm1 = RMSNorm(d, cfg.eps)
+        self.attn = ContinuumSelfAttention(d, cfg.n_heads, cfg.rope_theta, cfg.ca_query_tile, attention_fn)
+        self.norm2 = RMSNorm(d, cfg.eps)
+        self.mlp = GELUMLP(d, cfg.mlp_ratio)
+
+    def forward(self, x):
+        x = x + self.attn(self.norm1(x))
+        return x + self.mlp(self.norm2(x))
+
+
+class ContinuumDecoderLM(nn.Module):
+    """Byte-level decoder; ``forward(ids, targets=None) -> {'logits', 'loss'}``."""
+
+    def __init__(self, cfg: ContinuumDecoderConfig, attention_fn: Optional[Callable] = None):
+        super().__init__()
+        self.cfg = cfg
+        self.byte_emb = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        self.blocks = nn.ModuleList([CADecoderBlock(cfg, attention_fn) for _ in range(cfg.n_layers)])
+        self.norm_f = RMSNorm(cfg.d_model, cfg.eps)
+        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)   # not tied to byte_emb
+        self.residual_init_scale = 1.0 / math.sqrt(2.0 * cfg.n_layers)
+        self.apply(self._init_weights)
+
+    def _init_weights(self, m):
+        if isinstance(m, nn.Linear):
+            std = 0.02 * self.residual_init_scale if getattr(m, "_residual_proj", False) else 0.02
+            nn.init.normal_(m.weight, mean=0.0, std=std)
+        elif isinstance(m, nn.Embedding):
+            nn.init.normal_(m.weight, mean=0.0, std=0.02)
+
+    def forward(self, input_ids, targets=None):
+        if input_ids.dim() != 2 or input_ids.shape[1] > self.cfg.block_size:
+            raise ValueError("Input must be [B,T] with T<=block_size")
+        x = self.byte_emb(input_ids)
+        for block in self.blocks:
+            if self.cfg.grad_checkpointing and self.training:
+                x = torch.utils.checkpoint.checkpoint(block, x, use_reentrant=False)
+            else:
+                x = block(x)
+        logits = self.lm_head(self.norm_f(x))
+        out = {"logits": logits}
+        if targets is not None:
+            out["loss"] = F.cross_entropy(logits[:, :-1, :].reshape(-1, self.cfg.vocab_size),
+                                          targets[:, 1:].reshape(-1), reduction="mean")
+        return out
+
+
+def count_parameters(model: nn.Module) -> dict:
+    params = list(model.parameters())
+    return {"total": sum(p.numel() for p in params),
+            "trainable": sum(p.numel() for p in params if p.requires_grad)}
