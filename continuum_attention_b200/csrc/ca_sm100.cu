@@ -160,6 +160,63 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   mbar_wait(&sm.bar_o_done, 0, nab);
 }
 
+// P for 16 keys of one row: keys j0-1+c for c = 16*ch .. 16*ch+15 (P column c).
+// kEdge = the tile is the first key tile or the diagonal one (masking, caps);
+// interior tiles have every key visible and no caps.
+template <bool kBF16, bool kEdge>
+__device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, float scale, float m2, int nvis, int j0,
+                                          int i, float& sa, float& ea, float& bprev, float& z, uint32_t t_hi,
+                                          uint32_t t_lo) {
+  uint32_t hi[8], lo[8];
+#pragma unroll
+  for (int x = 0; x < 16; x += 2) {
+    float pv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = 16 * ch + x + u;
+      const float sb = __uint_as_float(cur[x + u]) * scale;
+      float M0, M1, eb;
+      if (kEdge) {
+        const bool vis = c < nvis;
+        eb = vis ? ex2_approx(fmaf(sb, kLog2e, -m2)) : 0.f;
+        seg_moments01_sel(ea, eb, sb - sa, M0, M1);
+        const bool seg_ok = vis && (j0 + c) >= 1;
+        M0 = seg_ok ? M0 : 0.f;
+        M1 = seg_ok ? M1 : 0.f;
+      } else {
+        eb = ex2_approx(fmaf(sb, kLog2e, -m2));
+        seg_moments01_sel(ea, eb, sb - sa, M0, M1);
+      }
+      float p = bprev + (M0 - M1);
+      z += M0;
+      if (kEdge && c >= 1) {
+        const int key = j0 - 1 + c;
+        const float cap = 0.5f * ea * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
+        p += cap;
+        z += cap;
+      }
+      pv[u] = p;
+      bprev = M1;
+      sa = sb;
+      ea = eb;
+    }
+    const uint32_t h2 = kBF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
+    float h0, h1;
+    if (kBF16) {
+      h0 = __uint_as_float(h2 << 16);
+      h1 = __uint_as_float(h2 & 0xffff0000u);
+    } else {
+      const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
+      h0 = __low2float(hh);
+      h1 = __high2float(hh);
+    }
+    hi[x / 2] = h2;
+    lo[x / 2] = kBF16 ? pack_bf16x2(pv[0] - h0, pv[1] - h1) : pack_f16x2(pv[0] - h0, pv[1] - h1);
+  }
+  tmem_st8(t_hi + 8 * ch, hi);
+  tmem_st8(t_lo + 8 * ch, lo);
+}
+
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32, float* stats,
                            int bh, int h, int Tn, int q0, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
@@ -182,6 +239,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     const int j0 = j * BN;
     const bool diag = (j == n_tiles - 1);
     const int nvis = diag ? min(i - j0 + 1, BN) : BN;
+    const bool edge = diag || j == 0;
     // pass 1: tile max over the visible keys
     uint32_t sr[2][32];
     float tmax = -INFINITY;
@@ -189,9 +247,14 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     for (int c = 0; c < 4; ++c) {
       tmem_ld32(tS + 32 * c, sr[0]);
       tmem_ld_wait();
+      if (diag) {
 #pragma unroll
-      for (int x = 0; x < 32; ++x)
-        if (32 * c + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[0][x]));
+        for (int x = 0; x < 32; ++x)
+          if (32 * c + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[0][x]));
+      } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) tmax = fmaxf(tmax, __uint_as_float(sr[0][x]));
+      }
     }
     tmax *= scale;
     const bool need = tmax > m_used + kRescaleNats;
@@ -217,60 +280,30 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     float ea = (j0 > 0) ? ex2_approx(fmaf(sprev, kLog2e, -m2)) : 0.f;
     float bprev = bpend;
     // pass 2: P for 16 keys at a time; the next chunk's load overlaps this chunk's math
-    auto chunk = [&](const uint32_t (&cur)[16], int ch) {
-      uint32_t hi[8], lo[8];
-#pragma unroll
-      for (int x = 0; x < 16; x += 2) {
-        float pv[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = 16 * ch + x + u;
-          const float sb = __uint_as_float(cur[x + u]) * scale;
-          const bool vis = c < nvis;
-          const float eb = vis ? ex2_approx(fmaf(sb, kLog2e, -m2)) : 0.f;
-          float M0, M1;
-          seg_moments01(ea, eb, sb - sa, M0, M1);
-          const bool seg_ok = vis && (j0 + c) >= 1;
-          float p = bprev + (seg_ok ? M0 - M1 : 0.f);
-          z += seg_ok ? M0 : 0.f;
-          if (c >= 1) {
-            const int key = j0 - 1 + c;
-            const float cap = 0.5f * ea * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
-            p += cap;
-            z += cap;
-          }
-          pv[u] = p;
-          bprev = seg_ok ? M1 : 0.f;
-          sa = sb;
-          ea = eb;
-        }
-        const uint32_t h2 = kBF16 ? pack_bf16x2(pv[0], pv[1]) : pack_f16x2(pv[0], pv[1]);
-        float h0, h1;
-        if (kBF16) {
-          h0 = __uint_as_float(h2 << 16);
-          h1 = __uint_as_float(h2 & 0xffff0000u);
-        } else {
-          const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
-          h0 = __low2float(hh);
-          h1 = __high2float(hh);
-        }
-        hi[x / 2] = h2;
-        lo[x / 2] = kBF16 ? pack_bf16x2(pv[0] - h0, pv[1] - h1) : pack_f16x2(pv[0] - h0, pv[1] - h1);
-      }
-      tmem_st8(tS + 8 * ch, hi);
-      tmem_st8(tmem + TMEM_PLO + lane_base + 8 * ch, lo);
-    };
+    const uint32_t t_lo = tmem + TMEM_PLO + lane_base;
     uint32_t bufA[16], bufB[16];
     tmem_ld16(tS, bufA);
     tmem_ld_wait();
+    if (edge) {
 #pragma unroll 1
-    for (int ch = 0; ch < 8; ch += 2) {
-      tmem_ld16(tS + 16 * (ch + 1), bufB);
-      chunk(bufA, ch);
-      tmem_ld_wait();
-      if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
-      chunk(bufB, ch + 1);
-      tmem_ld_wait();
+      for (int ch = 0; ch < 8; ch += 2) {
+        tmem_ld16(tS + 16 * (ch + 1), bufB);
+        fwd_chunk<kBF16, true>(bufA, ch, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
+        tmem_ld_wait();
+        if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
+        fwd_chunk<kBF16, true>(bufB, ch + 1, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
+        tmem_ld_wait();
+      }
+    } else {
+#pragma unroll 1
+      for (int ch = 0; ch < 8; ch += 2) {
+        tmem_ld16(tS + 16 * (ch + 1), bufB);
+        fwd_chunk<kBF16, false>(bufA, ch, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
+        tmem_ld_wait();
+        if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
+        fwd_chunk<kBF16, false>(bufB, ch + 1, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
+        tmem_ld_wait();
+      }
     }
     if (diag && i == j0 + BN - 1) {   // cap of key i sits in the last column: keep it pending
       bprev += 0.5f * ea;
@@ -546,6 +579,69 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   mbar_wait(&sm.bar_drain, 0, nab);
 }
 
+// dS and P for 16 consecutive keys of one query row.  On entry (sc, ec, gc) are
+// the score, exponential and g = dP - D of the current key (kfirst) and
+// (Rprev, Bprev) the right shares of the segment into it; sv/pv hold the raw
+// scores / dP of keys kfirst .. kfirst+15 (entry 0 is the current key), and
+// s_next / p_next those of key kfirst+16.  kEdge handles masking and caps.
+template <bool kBF16, bool kEdge>
+__device__ __forceinline__ void bwd_keys16(const uint32_t (&sv)[16], const uint32_t (&pv)[16], uint32_t s_next,
+                                           uint32_t p_next, int kfirst, int i, bool row_ok, float scale, float m2,
+                                           float dd, float iz, float& sc, float& ec, float& gc, float& Rprev,
+                                           float& Bprev, float& gsum, uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+#pragma unroll
+  for (int x = 0; x < 16; x += 2) {
+    float po[2], dso[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = x + u;
+      const int key = kfirst + c;
+      const uint32_t sn_bits = (c + 1 < 16) ? sv[(c + 1) & 15] : s_next;
+      const uint32_t pn_bits = (c + 1 < 16) ? pv[(c + 1) & 15] : p_next;
+      const float sn = __uint_as_float(sn_bits) * scale;
+      const float gn = __uint_as_float(pn_bits) - dd;
+      float en, M0, M1, M2;
+      bool vn = true;
+      if (kEdge) {
+        vn = row_ok && (key + 1) <= i;
+        en = vn ? ex2_approx(fmaf(sn, kLog2e, -m2)) : 0.f;
+      } else {
+        en = ex2_approx(fmaf(sn, kLog2e, -m2));
+      }
+      seg_moments012_sel(ec, en, sn - sc, M0, M1, M2);
+      if (kEdge) {
+        M0 = vn ? M0 : 0.f;
+        M1 = vn ? M1 : 0.f;
+        M2 = vn ? M2 : 0.f;
+      }
+      const float G = gn - gc;
+      const float Anext = M0 - M1;
+      const float Lnext = fmaf(gc, Anext, G * (M1 - M2));
+      const float Rn = fmaf(gc, M1, G * M2);
+      float ds, p;
+      if (kEdge) {
+        const bool vc = row_ok && key >= 0 && key <= i;
+        const float cap = 0.5f * ec * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
+        ds = vc ? (Rprev + Lnext + cap * gc) * iz : 0.f;
+        p = vc ? (Bprev + Anext + cap) * iz : 0.f;
+      } else {
+        ds = (Rprev + Lnext) * iz;
+        p = (Bprev + Anext) * iz;
+      }
+      gsum = fmaf(ds, sc, gsum);
+      po[u] = p;
+      dso[u] = ds * scale;
+      Rprev = Rn;
+      Bprev = M1;
+      sc = sn;
+      ec = en;
+      gc = gn;
+    }
+    pk[x / 2] = kBF16 ? pack_bf16x2(po[0], po[1]) : pack_f16x2(po[0], po[1]);
+    dk[x / 2] = kBF16 ? pack_bf16x2(dso[0], dso[1]) : pack_f16x2(dso[0], dso[1]);
+  }
+}
+
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
                            float* dq_acc, void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
@@ -579,93 +675,43 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
-    uint32_t s_lo, s_hi, p_lo, p_hi;
-    uint32_t sv[2][16], pv[2][16];
-    tmem_ld1(colS - 1, s_lo);
-    tmem_ld16(colS, sv[0]);
-    tmem_ld16(colS + 16, sv[1]);
-    tmem_ld1(colS + 32, s_hi);
-    tmem_ld1(colP - 1, p_lo);
-    tmem_ld16(colP, pv[0]);
-    tmem_ld16(colP + 16, pv[1]);
-    tmem_ld1(colP + 32, p_hi);
-    tmem_ld_wait();
-    tc_fence_before();
-    mbar_arrive(&sm.bar_s_consumed);
-
     const int kbase = j0 + 32 * qk;              // key of local column 0
     const float m2 = m * kLog2e;
-    auto vis = [&](int key) { return row_ok && key >= 0 && key <= i; };
-    auto E = [&](float s, int key) { return vis(key) ? ex2_approx(fmaf(s, kLog2e, -m2)) : 0.f; };
-    // left halo key kbase-1 and the segment into key kbase
+    // every key this thread touches is visible, inside [0, T) and capless: no masking needed
+    const bool interior = t >= 1 && kt >= 1 && (i0 + BM) <= Tn && (j0 + BN) < Tn;
+    // chunk 0: left halo, keys 0..15, key 16
+    uint32_t s_lo, p_lo, s16, p16, sv[16], pv[16];
+    tmem_ld1(colS - 1, s_lo);
+    tmem_ld16(colS, sv);
+    tmem_ld1(colS + 16, s16);
+    tmem_ld1(colP - 1, p_lo);
+    tmem_ld16(colP, pv);
+    tmem_ld1(colP + 16, p16);
+    tmem_ld_wait();
+    // the segment from the left halo key into key kbase
     float sa = __uint_as_float(s_lo) * scale;
-    float ea = E(sa, kbase - 1);
     float ga = __uint_as_float(p_lo) - dd;
-    float Rprev = 0.f, Bprev = 0.f;
-    float sc = __uint_as_float(sv[0][0]) * scale;
-    float ec = E(sc, kbase);
-    float gc = __uint_as_float(pv[0][0]) - dd;
-    if (vis(kbase) && kbase >= 1) {
+    float sc = __uint_as_float(sv[0]) * scale;
+    float gc = __uint_as_float(pv[0]) - dd;
+    float ea, ec, Rprev, Bprev;
+    {
+      const bool va = interior || (row_ok && kbase - 1 >= 0 && kbase - 1 <= i);
+      const bool vc = interior || (row_ok && kbase <= i);
+      ea = va ? ex2_approx(fmaf(sa, kLog2e, -m2)) : 0.f;
+      ec = vc ? ex2_approx(fmaf(sc, kLog2e, -m2)) : 0.f;
       float M0, M1, M2;
-      seg_moments012(ea, ec, sc - sa, M0, M1, M2);
+      seg_moments012_sel(ea, ec, sc - sa, M0, M1, M2);
+      const bool ok0 = vc && kbase >= 1;
       const float G = gc - ga;
-      Rprev = fmaf(ga, M1, G * M2);
-      Bprev = M1;
+      Rprev = ok0 ? fmaf(ga, M1, G * M2) : 0.f;
+      Bprev = ok0 ? M1 : 0.f;
     }
     if (t > 0) {
       const bool got2 = mbar_wait(&sm.bar_mma_done, (t - 1) & 1, ab);
       if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
     }
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      uint32_t pk[8], dk[8];
-#pragma unroll
-      for (int x = 0; x < 16; x += 2) {
-        float po[2], dso[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = 16 * ch + x + u;          // current key kbase + c
-          const int key = kbase + c;
-          // next key (c+1): from the register tile or the right halo
-          uint32_t sn_bits, pn_bits;
-          if (c + 1 < 32) {
-            sn_bits = sv[(c + 1) >> 4][(c + 1) & 15];
-            pn_bits = pv[(c + 1) >> 4][(c + 1) & 15];
-          } else {
-            sn_bits = s_hi;
-            pn_bits = p_hi;
-          }
-          const float sn = __uint_as_float(sn_bits) * scale;
-          const float en = E(sn, key + 1);
-          const float gn = __uint_as_float(pn_bits) - dd;
-          float Lnext = 0.f, Anext = 0.f, Rn = 0.f, Bn = 0.f;
-          if (vis(key + 1)) {
-            float M0, M1, M2;
-            seg_moments012(ec, en, sn - sc, M0, M1, M2);
-            const float G = gn - gc;
-            Anext = M0 - M1;
-            Lnext = fmaf(gc, Anext, G * (M1 - M2));
-            Rn = fmaf(gc, M1, G * M2);
-            Bn = M1;
-          }
-          float ds = 0.f, p = 0.f;
-          if (vis(key)) {
-            const float cap = 0.5f * ec * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
-            ds = (Rprev + Lnext + cap * gc) * iz;
-            p = (Bprev + Anext + cap) * iz;
-            gsum = fmaf(ds, sc, gsum);
-          }
-          po[u] = p;
-          dso[u] = ds * scale;
-          Rprev = Rn;
-          Bprev = Bn;
-          sc = sn;
-          ec = en;
-          gc = gn;
-        }
-        pk[x / 2] = kBF16 ? pack_bf16x2(po[0], po[1]) : pack_f16x2(po[0], po[1]);
-        dk[x / 2] = kBF16 ? pack_bf16x2(dso[0], dso[1]) : pack_f16x2(dso[0], dso[1]);
-      }
+    uint32_t pk[8], dk[8];
+    auto store16 = [&](int ch) {
       // two 16-byte chunks of this row (8 keys each), 128-byte swizzle: chunk ^ (row & 7)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -674,7 +720,30 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
         *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
         *reinterpret_cast<uint4*>(dbuf + off) = make_uint4(dk[4 * hh], dk[4 * hh + 1], dk[4 * hh + 2], dk[4 * hh + 3]);
       }
-    }
+    };
+    if (interior)
+      bwd_keys16<kBF16, false>(sv, pv, s16, p16, kbase, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev, Bprev,
+                               gsum, pk, dk);
+    else
+      bwd_keys16<kBF16, true>(sv, pv, s16, p16, kbase, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev, Bprev,
+                              gsum, pk, dk);
+    store16(0);
+    // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
+    uint32_t s_hi, p_hi;
+    tmem_ld16(colS + 16, sv);
+    tmem_ld1(colS + 32, s_hi);
+    tmem_ld16(colP + 16, pv);
+    tmem_ld1(colP + 32, p_hi);
+    tmem_ld_wait();
+    tc_fence_before();
+    mbar_arrive(&sm.bar_s_consumed);
+    if (interior)
+      bwd_keys16<kBF16, false>(sv, pv, s_hi, p_hi, kbase + 16, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev,
+                               Bprev, gsum, pk, dk);
+    else
+      bwd_keys16<kBF16, true>(sv, pv, s_hi, p_hi, kbase + 16, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev,
+                              Bprev, gsum, pk, dk);
+    store16(1);
     // dQ of the previous query tile: TMEM -> fp32 accumulator in global memory
     if (t > 0) {
       uint32_t qv[16];
