@@ -244,16 +244,20 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     uint32_t sr[2][32];
     float tmax = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 4; c += 2) {
       tmem_ld32(tS + 32 * c, sr[0]);
+      tmem_ld32(tS + 32 * (c + 1), sr[1]);
       tmem_ld_wait();
-      if (diag) {
 #pragma unroll
-        for (int x = 0; x < 32; ++x)
-          if (32 * c + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[0][x]));
-      } else {
+      for (int hh = 0; hh < 2; ++hh) {
+        if (diag) {
 #pragma unroll
-        for (int x = 0; x < 32; ++x) tmax = fmaxf(tmax, __uint_as_float(sr[0][x]));
+          for (int x = 0; x < 32; ++x)
+            if (32 * (c + hh) + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[hh][x]));
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) tmax = fmaxf(tmax, __uint_as_float(sr[hh][x]));
+        }
       }
     }
     tmax *= scale;
@@ -579,27 +583,33 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   mbar_wait(&sm.bar_drain, 0, nab);
 }
 
-// dS and P for 16 consecutive keys of one query row.  On entry (sc, ec, gc) are
-// the score, exponential and g = dP - D of the current key (kfirst) and
-// (Rprev, Bprev) the right shares of the segment into it; sv/pv hold the raw
-// scores / dP of keys kfirst .. kfirst+15 (entry 0 is the current key), and
-// s_next / p_next those of key kfirst+16.  kEdge handles masking and caps.
+// scale*dS and P for 8 consecutive keys of one query row, packed as 16-bit pairs.
+// The exponentials are taken against m + ln Z (E = e^{s-m}/Z), so every moment,
+// and with it P and dS, comes out normalised; g = (dP - D) * scale, so the
+// result is the scale*dS the dK/dQ products need.  On entry (sc, ec, gc) belong
+// to the current key (kfirst) and (Rprev, Bprev) are the right shares of the
+// segment into it; sv/pv[off .. off+7] hold the raw scores / dP of keys
+// kfirst .. kfirst+7 (entry off is the current key) and the next key's come
+// from sv/pv[off+8] or, past the end, from s_next / p_next.  gsum collects
+// scale * sum dS*s.  kEdge handles masking and caps.
 template <bool kBF16, bool kEdge>
-__device__ __forceinline__ void bwd_keys16(const uint32_t (&sv)[16], const uint32_t (&pv)[16], uint32_t s_next,
-                                           uint32_t p_next, int kfirst, int i, bool row_ok, float scale, float m2,
-                                           float dd, float iz, float& sc, float& ec, float& gc, float& Rprev,
-                                           float& Bprev, float& gsum, uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+__device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32_t (&pv)[16], int off,
+                                          uint32_t s_next, uint32_t p_next, int kfirst, int i, bool row_ok,
+                                          float scale, float m2, float dds, float& sc, float& ec, float& gc,
+                                          float& Rprev, float& Bprev, float& gsum, uint32_t (&pk)[4],
+                                          uint32_t (&dk)[4]) {
 #pragma unroll
-  for (int x = 0; x < 16; x += 2) {
+  for (int x = 0; x < 8; x += 2) {
     float po[2], dso[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int c = x + u;
       const int key = kfirst + c;
-      const uint32_t sn_bits = (c + 1 < 16) ? sv[(c + 1) & 15] : s_next;
-      const uint32_t pn_bits = (c + 1 < 16) ? pv[(c + 1) & 15] : p_next;
+      const int nxt = off + c + 1;
+      const uint32_t sn_bits = (nxt < 16) ? sv[nxt & 15] : s_next;
+      const uint32_t pn_bits = (nxt < 16) ? pv[nxt & 15] : p_next;
       const float sn = __uint_as_float(sn_bits) * scale;
-      const float gn = __uint_as_float(pn_bits) - dd;
+      const float gn = fmaf(__uint_as_float(pn_bits), scale, -dds);
       float en, M0, M1, M2;
       bool vn = true;
       if (kEdge) {
@@ -622,15 +632,15 @@ __device__ __forceinline__ void bwd_keys16(const uint32_t (&sv)[16], const uint3
       if (kEdge) {
         const bool vc = row_ok && key >= 0 && key <= i;
         const float cap = 0.5f * ec * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
-        ds = vc ? (Rprev + Lnext + cap * gc) * iz : 0.f;
-        p = vc ? (Bprev + Anext + cap) * iz : 0.f;
+        ds = vc ? fmaf(cap, gc, Rprev + Lnext) : 0.f;
+        p = vc ? Bprev + Anext + cap : 0.f;
       } else {
-        ds = (Rprev + Lnext) * iz;
-        p = (Bprev + Anext) * iz;
+        ds = Rprev + Lnext;
+        p = Bprev + Anext;
       }
       gsum = fmaf(ds, sc, gsum);
       po[u] = p;
-      dso[u] = ds * scale;
+      dso[u] = ds;
       Rprev = Rn;
       Bprev = M1;
       sc = sn;
@@ -640,6 +650,14 @@ __device__ __forceinline__ void bwd_keys16(const uint32_t (&sv)[16], const uint3
     pk[x / 2] = kBF16 ? pack_bf16x2(po[0], po[1]) : pack_f16x2(po[0], po[1]);
     dk[x / 2] = kBF16 ? pack_bf16x2(dso[0], dso[1]) : pack_f16x2(dso[0], dso[1]);
   }
+}
+
+// one 16-byte chunk (8 keys) of a query row; 128-byte swizzle: chunk ^ (row & 7)
+__device__ __forceinline__ void store_chunk(uint8_t* prow, uint8_t* drow, int chunk, int swz,
+                                            const uint32_t (&pk)[4], const uint32_t (&dk)[4]) {
+  const uint32_t off = (uint32_t)((chunk ^ swz) * 16);
+  *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  *reinterpret_cast<uint4*>(drow + off) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
 }
 
 template <bool kBF16>
@@ -661,22 +679,31 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   float gsum = 0.f;
   bool ok = true;
 
+  // row statistics of the next query tile are loaded one iteration ahead
+  float nm = 0.f, nz = 1.f, nd = 0.f;
+  if (j0 + r < Tn) {
+    const size_t ri = (size_t)bh * Tn + j0 + r;
+    nm = stats[2 * ri];
+    nz = stats[2 * ri + 1];
+    nd = rowdot[ri];
+  }
   for (int t = 0; t < n_tiles; ++t) {
     const int i0 = j0 + t * BM;
     const int i = i0 + r;
     const bool row_ok = i < Tn;
-    float m = 0.f, iz = 0.f, dd = 0.f;
-    if (row_ok) {
-      const size_t ri = (size_t)bh * Tn + i;
-      m = stats[2 * ri];
-      iz = 1.f / stats[2 * ri + 1];
-      dd = rowdot[ri];
+    const float m = nm, zrow = nz, dd = nd;
+    if (t + 1 < n_tiles && i + BM < Tn) {
+      const size_t ri = (size_t)bh * Tn + i + BM;
+      nm = stats[2 * ri];
+      nz = stats[2 * ri + 1];
+      nd = rowdot[ri];
     }
     const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
     const int kbase = j0 + 32 * qk;              // key of local column 0
-    const float m2 = m * kLog2e;
+    const float m2 = row_ok ? fmaf(m, kLog2e, log2f(zrow)) : 0.f;   // E = e^{s-m} / Z
+    const float dds = dd * scale;
     // every key this thread touches is visible, inside [0, T) and capless: no masking needed
     const bool interior = t >= 1 && kt >= 1 && (i0 + BM) <= Tn && (j0 + BN) < Tn;
     // chunk 0: left halo, keys 0..15, key 16
@@ -690,9 +717,9 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     tmem_ld_wait();
     // the segment from the left halo key into key kbase
     float sa = __uint_as_float(s_lo) * scale;
-    float ga = __uint_as_float(p_lo) - dd;
+    float ga = fmaf(__uint_as_float(p_lo), scale, -dds);
     float sc = __uint_as_float(sv[0]) * scale;
-    float gc = __uint_as_float(pv[0]) - dd;
+    float gc = fmaf(__uint_as_float(pv[0]), scale, -dds);
     float ea, ec, Rprev, Bprev;
     {
       const bool va = interior || (row_ok && kbase - 1 >= 0 && kbase - 1 <= i);
@@ -706,28 +733,24 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
       Rprev = ok0 ? fmaf(ga, M1, G * M2) : 0.f;
       Bprev = ok0 ? M1 : 0.f;
     }
+    uint8_t* const prow = pbuf + (uint32_t)r * 128;
+    uint8_t* const drow = dbuf + (uint32_t)r * 128;
+    const int swz = r & 7;
+    uint32_t pk[4], dk[4];
+#define CA_KEYS8(EDGE, OFF, SN, PN, KF)                                                                   \
+  bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Rprev, Bprev, gsum, pk, dk)
+    // keys 0..7 are computed before waiting for the previous tile's dV/dK/dQ products,
+    // which still read the shared P/dS buffer; their latency hides behind this work
+    if (interior) CA_KEYS8(false, 0, s16, p16, kbase);
+    else CA_KEYS8(true, 0, s16, p16, kbase);
     if (t > 0) {
       const bool got2 = mbar_wait(&sm.bar_mma_done, (t - 1) & 1, ab);
       if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
     }
-    uint32_t pk[8], dk[8];
-    auto store16 = [&](int ch) {
-      // two 16-byte chunks of this row (8 keys each), 128-byte swizzle: chunk ^ (row & 7)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int chunk = chunk0 + 2 * ch + hh;
-        const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) * 16);
-        *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
-        *reinterpret_cast<uint4*>(dbuf + off) = make_uint4(dk[4 * hh], dk[4 * hh + 1], dk[4 * hh + 2], dk[4 * hh + 3]);
-      }
-    };
-    if (interior)
-      bwd_keys16<kBF16, false>(sv, pv, s16, p16, kbase, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev, Bprev,
-                               gsum, pk, dk);
-    else
-      bwd_keys16<kBF16, true>(sv, pv, s16, p16, kbase, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev, Bprev,
-                              gsum, pk, dk);
-    store16(0);
+    store_chunk(prow, drow, chunk0, swz, pk, dk);
+    if (interior) CA_KEYS8(false, 8, s16, p16, kbase + 8);
+    else CA_KEYS8(true, 8, s16, p16, kbase + 8);
+    store_chunk(prow, drow, chunk0 + 1, swz, pk, dk);
     // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
     uint32_t s_hi, p_hi;
     tmem_ld16(colS + 16, sv);
@@ -737,13 +760,13 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     tmem_ld_wait();
     tc_fence_before();
     mbar_arrive(&sm.bar_s_consumed);
-    if (interior)
-      bwd_keys16<kBF16, false>(sv, pv, s_hi, p_hi, kbase + 16, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev,
-                               Bprev, gsum, pk, dk);
-    else
-      bwd_keys16<kBF16, true>(sv, pv, s_hi, p_hi, kbase + 16, i, row_ok, scale, m2, dd, iz, sc, ec, gc, Rprev,
-                              Bprev, gsum, pk, dk);
-    store16(1);
+    if (interior) CA_KEYS8(false, 0, s_hi, p_hi, kbase + 16);
+    else CA_KEYS8(true, 0, s_hi, p_hi, kbase + 16);
+    store_chunk(prow, drow, chunk0 + 2, swz, pk, dk);
+    if (interior) CA_KEYS8(false, 8, s_hi, p_hi, kbase + 24);
+    else CA_KEYS8(true, 8, s_hi, p_hi, kbase + 24);
+    store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
+#undef CA_KEYS8
     // dQ of the previous query tile: TMEM -> fp32 accumulator in global memory
     if (t > 0) {
       uint32_t qv[16];
@@ -803,7 +826,8 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
       }
     }
   }
-  // d log_gain partial of this key tile: sum over the CTA of dS * s
+  // d log_gain partial of this key tile: sum over the CTA of dS * s (gsum holds scale * that)
+  gsum /= scale;
   for (int off = 16; off > 0; off >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, off);
   if (lane == 0) sm.red[warp] = gsum;
   named_bar_sync(1, NUM_MATH_WARPS * 32);
