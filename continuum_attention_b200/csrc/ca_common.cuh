@@ -113,39 +113,11 @@ __device__ __forceinline__ void seg_moments012(float Ea, float Eb, float d, floa
 
 // ---------------------------------------------------------------------------
 // Branch-free variants for the bf16/f16 tensor-core kernels.  Both the closed
-// form and a shorter series are evaluated and one is selected, so consecutive
+// form and a short series are evaluated and one is selected, so consecutive
 // keys carry no divergent branch and the compiler can interleave them.  The
-// series covers |d| < kSeriesMaxLowp with eight terms (truncation below 1e-8);
-// above it the closed forms lose at most ~2e-6 (M1) and ~1e-5 (M2) relative,
-// far inside the bf16/f16 error budget.  The fp32 SIMT path keeps the more
-// accurate threshold of 1 above.
-constexpr float kSeriesMaxLowp = 0.5f;
-
-// sum_{k<8} d^k / (k! (k+2))
-__device__ __forceinline__ float series_j1_short(float d) {
-  float p = 1.f / 45360.f;
-  p = fmaf(p, d, 1.f / 5760.f);
-  p = fmaf(p, d, 1.f / 840.f);
-  p = fmaf(p, d, 1.f / 144.f);
-  p = fmaf(p, d, 1.f / 30.f);
-  p = fmaf(p, d, 1.f / 8.f);
-  p = fmaf(p, d, 1.f / 3.f);
-  p = fmaf(p, d, 1.f / 2.f);
-  return p;
-}
-
-// sum_{k<8} d^k / (k! (k+3))
-__device__ __forceinline__ float series_j2_short(float d) {
-  float p = 1.f / 50400.f;
-  p = fmaf(p, d, 1.f / 6480.f);
-  p = fmaf(p, d, 1.f / 960.f);
-  p = fmaf(p, d, 1.f / 168.f);
-  p = fmaf(p, d, 1.f / 36.f);
-  p = fmaf(p, d, 1.f / 10.f);
-  p = fmaf(p, d, 1.f / 4.f);
-  p = fmaf(p, d, 1.f / 3.f);
-  return p;
-}
+// thresholds trade closed-form cancellation against series length; their
+// errors stay far inside the bf16/f16 budget.  The fp32 SIMT path keeps the
+// more accurate threshold of 1 above.
 
 // Forward-only threshold: M1 from the closed form loses ~2 eps / d^2 relative,
 // 6e-6 at |d| = 0.25; six series terms then truncate below 5e-8.
@@ -173,16 +145,32 @@ __device__ __forceinline__ void seg_moments01_sel(float Ea, float Eb, float d, f
   M1 = small ? m1s : m1c;
 }
 
+// Backward threshold: M2 from the closed form loses ~1.4e-6 / |d|^3 relative
+// (9e-5 at |d| = 0.25, on the few keys near the threshold); six series terms
+// then truncate below 4e-8.
+constexpr float kSeriesMaxBwd = 0.25f;
+
+// sum_{k<6} d^k / (k! (k+3))
+__device__ __forceinline__ float series_j2_bwd(float d) {
+  float p = 1.f / 960.f;
+  p = fmaf(p, d, 1.f / 168.f);
+  p = fmaf(p, d, 1.f / 36.f);
+  p = fmaf(p, d, 1.f / 10.f);
+  p = fmaf(p, d, 1.f / 4.f);
+  p = fmaf(p, d, 1.f / 3.f);
+  return p;
+}
+
 __device__ __forceinline__ void seg_moments012_sel(float Ea, float Eb, float d, float& M0, float& M1,
                                                    float& M2) {
   const float r = rcp_approx(d);
   const float m0c = (Eb - Ea) * r;
   const float m1c = (Eb - m0c) * r;
   const float m2c = fmaf(-2.f, m1c, Eb) * r;
-  const float m2s = Ea * series_j2_short(d);
+  const float m2s = Ea * series_j2_bwd(d);
   const float m1s = 0.5f * fmaf(-d, m2s, Eb);
   const float m0s = fmaf(-d, m1s, Eb);
-  const bool small = fabsf(d) < kSeriesMaxLowp;
+  const bool small = fabsf(d) < kSeriesMaxBwd;
   M0 = small ? m0s : m0c;
   M1 = small ? m1s : m1c;
   M2 = small ? m2s : m2c;

@@ -494,6 +494,57 @@ __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ do
   if (lane == 0) rowdot[row] = s;
 }
 
+// Backward preparation for D = 64, one pass: D_i = dO_i . O_i and zeros for the
+// fp32 dQ accumulator.  16 threads per row, 4 consecutive elements each
+// (16-byte O loads when O is fp32, 8-byte dO loads), 2 rows per warp.
+template <typename TO, typename T>
+__global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ dout, float* __restrict__ rowdot,
+                              float* __restrict__ dq_acc, size_t rows) {
+  const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t row = gid >> 4;
+  const int part = (int)(gid & 15);
+  float s = 0.f;
+  if (row < rows) {
+    const size_t base = row * 64 + 4 * part;
+    float ov[4], dv[4];
+    if (sizeof(TO) == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(o) + base);
+      ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ov[u] = to_f32(o[base + u]);
+    }
+    if (sizeof(T) == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(dout) + base);
+      dv[0] = x.x; dv[1] = x.y; dv[2] = x.z; dv[3] = x.w;
+    } else {
+      const uint2 raw = *reinterpret_cast<const uint2*>(dout + base);
+      const T* dp = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dv[u] = to_f32(dp[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) s = fmaf(ov[u], dv[u], s);
+    *reinterpret_cast<float4*>(dq_acc + base) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (row < rows && part == 0) rowdot[row] = s;
+}
+
+// fp32 -> dtype, 4 elements per thread (n a multiple of 4, 16-byte aligned source)
+template <typename T>
+__global__ void cast4_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n4) {
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n4; idx += (size_t)gridDim.x * blockDim.x) {
+    const float4 x = reinterpret_cast<const float4*>(src)[idx];
+    T out[4] = {from_f32<T>(x.x), from_f32<T>(x.y), from_f32<T>(x.z), from_f32<T>(x.w)};
+    if (sizeof(T) == 2)
+      reinterpret_cast<uint2*>(dst)[idx] = *reinterpret_cast<const uint2*>(out);
+    else
+      reinterpret_cast<float4*>(dst)[idx] = *reinterpret_cast<const float4*>(out);
+  }
+}
+
 template <typename T>
 __global__ void cast_rows_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n) {
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
@@ -580,19 +631,43 @@ static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_rowdot(const BwdArgs& a, float* rowdot) {
+template <typename T>
+static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc) {
+  const size_t rows = (size_t)a.B * a.H * a.T;
+  const uintptr_t oal = reinterpret_cast<uintptr_t>(a.o_f32 ? (const void*)a.o_f32 : a.o);
+  const bool vec = a.D == 64 && (reinterpret_cast<uintptr_t>(a.d_o) & (4 * sizeof(T) - 1)) == 0 &&
+                   (a.o_f32 || sizeof(T) == 4 ? (oal & 15) == 0 : true);
+  if (!vec) {
+    cudaError_t e = rowdot_dtype<T>(a, rowdot);
+    if (e != cudaSuccess) return e;
+    return cudaMemsetAsync(dq_acc, 0, rows * a.D * sizeof(float), a.stream);
+  }
+  const unsigned blocks = (unsigned)((rows * 16 + 255) / 256);
+  if (a.o_f32)
+    prep64_kernel<float, T><<<blocks, 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o, rowdot, dq_acc, rows);
+  else
+    prep64_kernel<T, T><<<blocks, 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o, rowdot, dq_acc, rows);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc) {
   switch (a.dtype) {
-    case 0: return rowdot_dtype<float>(a, rowdot);
-    case 1: return rowdot_dtype<__nv_bfloat16>(a, rowdot);
-    default: return rowdot_dtype<__half>(a, rowdot);
+    case 0: return prep_dtype<float>(a, rowdot, dq_acc);
+    case 1: return prep_dtype<__nv_bfloat16>(a, rowdot, dq_acc);
+    default: return prep_dtype<__half>(a, rowdot, dq_acc);
   }
 }
 
 template <typename T>
 static cudaError_t cast_dtype(const BwdArgs& a, const float* dq_acc) {
   const size_t n = (size_t)a.B * a.H * a.T * a.D;
-  cast_rows_kernel<T><<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
-      dq_acc, (T*)a.dq, n);
+  if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.dq) & (4 * sizeof(T) - 1)) == 0) {
+    cast4_kernel<T><<<(unsigned)std::min<size_t>((n / 4 + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
+        dq_acc, (T*)a.dq, n / 4);
+  } else {
+    cast_rows_kernel<T><<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
+        dq_acc, (T*)a.dq, n);
+  }
   return cudaGetLastError();
 }
 
@@ -611,10 +686,7 @@ cudaError_t launch_gain_reduce(const BwdArgs& a, const float* part, int nparts) 
 
 template <typename T>
 static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
-  const size_t rows = (size_t)a.B * a.H * a.T;
-  cudaError_t e = launch_rowdot(a, w.rowdot);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(w.dq_acc, 0, rows * a.D * sizeof(float), a.stream);
+  cudaError_t e = launch_prep(a, w.rowdot, w.dq_acc);
   if (e != cudaSuccess) return e;
   if (a.D <= 32) e = launch_bwd<T, 32>(a, w);
   else if (a.D <= 64) e = launch_bwd<T, 64>(a, w);

@@ -626,8 +626,9 @@ __device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32
       }
       const float G = gn - gc;
       const float Anext = M0 - M1;
-      const float Lnext = fmaf(gc, Anext, G * (M1 - M2));
-      const float Rn = fmaf(gc, M1, G * M2);
+      const float GM2 = G * M2;
+      const float Lnext = fmaf(gc, Anext, fmaf(G, M1, -GM2));   // g_c (M0-M1) + G (M1-M2)
+      const float Rn = fmaf(gc, M1, GM2);                       // g_c M1 + G M2
       float ds, p;
       if (kEdge) {
         const bool vc = row_ok && key >= 0 && key <= i;
@@ -968,9 +969,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM) ||
       !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH))
     return cudaErrorInvalidValue;
-  cudaError_t e = simt::launch_rowdot(a, w.rowdot);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(w.dq_acc, 0, (size_t)BH * a.T * a.D * sizeof(float), a.stream);
+  cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc);
   if (e != cudaSuccess) return e;
   auto kern = bwd::bwd_kernel<kBF16>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
