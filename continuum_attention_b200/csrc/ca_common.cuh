@@ -54,6 +54,13 @@ template <> __device__ __forceinline__ float from_f32<float>(float x) { return x
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions): one instruction computes both
+// lanes, each rounded exactly like its scalar counterpart.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
+
 // J_1(d) by its power series: sum_{k<10} d^k / (k! (k+2)).
 __device__ __forceinline__ float series_j1(float d) {
   float p = 1.f / 3991680.f;
@@ -120,13 +127,14 @@ __device__ __forceinline__ void seg_moments012(float Ea, float Eb, float d, floa
 // more accurate threshold of 1 above.
 
 // Forward-only threshold: M1 from the closed form loses ~2 eps / d^2 relative,
-// 6e-6 at |d| = 0.25; six series terms then truncate below 5e-8.
-constexpr float kSeriesMaxFwd = 0.25f;
+// 8e-6 at |d| = 0.125; five series terms then truncate below 4e-8.  Only M1 is
+// selected; M0 = Eb - d M1 holds for both branches (exactly for the series, and
+// for the closed form up to the rounding of M1).
+constexpr float kSeriesMaxFwd = 0.125f;
 
-// sum_{k<6} d^k / (k! (k+2))
+// sum_{k<5} d^k / (k! (k+2))
 __device__ __forceinline__ float series_j1_fwd(float d) {
-  float p = 1.f / 840.f;
-  p = fmaf(p, d, 1.f / 144.f);
+  float p = 1.f / 144.f;
   p = fmaf(p, d, 1.f / 30.f);
   p = fmaf(p, d, 1.f / 8.f);
   p = fmaf(p, d, 1.f / 3.f);
@@ -139,10 +147,8 @@ __device__ __forceinline__ void seg_moments01_sel(float Ea, float Eb, float d, f
   const float m0c = (Eb - Ea) * r;
   const float m1c = (Eb - m0c) * r;
   const float m1s = Ea * series_j1_fwd(d);
-  const float m0s = fmaf(-d, m1s, Eb);
-  const bool small = fabsf(d) < kSeriesMaxFwd;
-  M0 = small ? m0s : m0c;
-  M1 = small ? m1s : m1c;
+  M1 = fabsf(d) < kSeriesMaxFwd ? m1s : m1c;
+  M0 = fmaf(-d, M1, Eb);
 }
 
 // Backward threshold: M2 from the closed form loses ~1.4e-6 / |d|^3 relative
@@ -161,6 +167,8 @@ __device__ __forceinline__ float series_j2_bwd(float d) {
   return p;
 }
 
+// Only M2 is selected; M1 and M0 follow from the downward recurrence, which is
+// exact for the series and reproduces the closed form up to rounding.
 __device__ __forceinline__ void seg_moments012_sel(float Ea, float Eb, float d, float& M0, float& M1,
                                                    float& M2) {
   const float r = rcp_approx(d);
@@ -168,12 +176,9 @@ __device__ __forceinline__ void seg_moments012_sel(float Ea, float Eb, float d, 
   const float m1c = (Eb - m0c) * r;
   const float m2c = fmaf(-2.f, m1c, Eb) * r;
   const float m2s = Ea * series_j2_bwd(d);
-  const float m1s = 0.5f * fmaf(-d, m2s, Eb);
-  const float m0s = fmaf(-d, m1s, Eb);
-  const bool small = fabsf(d) < kSeriesMaxBwd;
-  M0 = small ? m0s : m0c;
-  M1 = small ? m1s : m1c;
-  M2 = small ? m2s : m2c;
+  M2 = fabsf(d) < kSeriesMaxBwd ? m2s : m2c;
+  M1 = 0.5f * fmaf(-d, M2, Eb);
+  M0 = fmaf(-d, M1, Eb);
 }
 
 }  // namespace ca
