@@ -217,6 +217,86 @@ __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, flo
   tmem_st8(t_lo + 8 * ch, lo);
 }
 
+// Interior chunk (every key visible, no caps) in packed fp32 pairs: lanes x/y
+// are the adjacent keys c = 16*ch + 2x, 2x+1.  Quantities that pair a key with
+// its left neighbour (score difference, Ea - Eb, Ea * series) use scalar ops, so
+// no register shuffling is needed.  Working with nd = -(b - a) keeps every
+// result bit-identical to seg_moments01_sel: rcp(nd) = -1/d exactly, and the
+// series constants carry the alternating signs.
+template <bool kBF16>
+__device__ __forceinline__ void fwd_chunk_fast(const uint32_t (&cur)[16], int ch, float2 scale2, float2 nm2,
+                                               float& sa, float& ea, float& bprev, float2& z2, uint32_t t_hi,
+                                               uint32_t t_lo) {
+  const float2 l2e = splat2(kLog2e), neg1 = splat2(-1.f);
+  uint32_t hi[8], lo[8];
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {
+    const float2 raw = make_float2(__uint_as_float(cur[2 * x]), __uint_as_float(cur[2 * x + 1]));
+    const float2 sb = mul2(raw, scale2);
+    const float2 arg = fma2(sb, l2e, nm2);
+    const float2 eb = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+    const float2 nd = make_float2(sa - sb.x, sb.x - sb.y);
+    const float2 rn = make_float2(rcp_approx(nd.x), rcp_approx(nd.y));
+    const float2 m0c = mul2(make_float2(ea - eb.x, eb.x - eb.y), rn);
+    const float2 m1c = mul2(fma2(eb, neg1, m0c), rn);
+    float2 ps = fma2(splat2(1.f / 144.f), nd, splat2(-1.f / 30.f));
+    ps = fma2(ps, nd, splat2(1.f / 8.f));
+    ps = fma2(ps, nd, splat2(-1.f / 3.f));
+    ps = fma2(ps, nd, splat2(1.f / 2.f));
+    float2 M1;
+    M1.x = fabsf(nd.x) < kSeriesMaxFwd ? ea * ps.x : m1c.x;
+    M1.y = fabsf(nd.y) < kSeriesMaxFwd ? eb.x * ps.y : m1c.y;
+    const float2 M0 = fma2(nd, M1, eb);
+    const float2 A = fma2(M1, neg1, M0);
+    const float pv0 = bprev + A.x, pv1 = M1.x + A.y;
+    z2 = add2(z2, M0);
+    bprev = M1.y;
+    sa = sb.y;
+    ea = eb.y;
+    const uint32_t h2 = kBF16 ? pack_bf16x2(pv0, pv1) : pack_f16x2(pv0, pv1);
+    float h0, h1;
+    if (kBF16) {
+      h0 = __uint_as_float(h2 << 16);
+      h1 = __uint_as_float(h2 & 0xffff0000u);
+    } else {
+      const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
+      h0 = __low2float(hh);
+      h1 = __high2float(hh);
+    }
+    hi[x] = h2;
+    lo[x] = kBF16 ? pack_bf16x2(pv0 - h0, pv1 - h1) : pack_f16x2(pv0 - h0, pv1 - h1);
+  }
+  tmem_st8(t_hi + 8 * ch, hi);
+  tmem_st8(t_lo + 8 * ch, lo);
+}
+
+// A chunk past every row's diagonal: all weights are zero.
+__device__ __forceinline__ void fwd_chunk_zero(int ch, float& ea, float& bprev, uint32_t t_hi, uint32_t t_lo) {
+  uint32_t zz[8];
+#pragma unroll
+  for (int x = 0; x < 8; ++x) zz[x] = 0u;
+  tmem_st8(t_hi + 8 * ch, zz);
+  tmem_st8(t_lo + 8 * ch, zz);
+  ea = 0.f;
+  bprev = 0.f;
+}
+
+// Which path chunk ch of this warp's rows takes: 0 = all zero, 1 = interior,
+// 2 = edge (masking and caps).  P column c of key tile j0 holds key j0+c-1 and
+// closes the segment into key j0+c.  On the diagonal tile (j0 = q0) the warp's
+// rows are i = q0+32w .. q0+32w+31: every segment of chunk ch is visible to all
+// of them, with no cap, when 16ch+15 <= 32w (ch < 2w); a row's last nonzero
+// column is i-j0+1 (its own key, half cap), so the chunk is zero for every row
+// when 16ch > 32w+32.  Chunk 0 of key tile 0 holds key 0 (cap) and the empty
+// segment before it.
+__device__ __forceinline__ int fwd_chunk_kind(int ch, int warp, bool diag, bool first) {
+  if (first && ch == 0) return 2;
+  if (!diag) return 1;
+  if (ch < 2 * warp) return 1;
+  if (16 * ch > 32 * warp + 32) return 0;
+  return 2;
+}
+
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32, float* stats,
                            int bh, int h, int Tn, int q0, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
@@ -231,6 +311,8 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   const uint32_t tO = tmem + TMEM_O + lane_base;
 
   float m_used = -INFINITY, z = 0.f, bpend = 0.f, sprev = 0.f;
+  float2 z2 = splat2(0.f);   // packed partial of z from interior chunks
+  const float2 scale2 = splat2(scale);
   bool ok = true;
   for (int j = 0; j < n_tiles; ++j) {
     const bool got = mbar_wait(&sm.bar_s_full, j & 1, ab);
@@ -268,6 +350,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
       const float m_new = need ? tmax : m_used;
       const float alpha = exp_rel(m_used - m_new);
       z *= alpha;
+      z2 = mul2(z2, splat2(alpha));
       bpend *= alpha;
       m_used = m_new;
 #pragma unroll
@@ -285,30 +368,27 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     float bprev = bpend;
     // pass 2: P for 16 keys at a time; the next chunk's load overlaps this chunk's math
     const uint32_t t_lo = tmem + TMEM_PLO + lane_base;
+    const float2 nm2 = splat2(-m2);
     uint32_t bufA[16], bufB[16];
     tmem_ld16(tS, bufA);
     tmem_ld_wait();
-    if (edge) {
+#define CA_FWD_CHUNK(BUF, CH)                                                                    \
+  {                                                                                              \
+    const int kind = fwd_chunk_kind(CH, warp, diag, j == 0);                                     \
+    if (kind == 1) fwd_chunk_fast<kBF16>(BUF, CH, scale2, nm2, sa, ea, bprev, z2, tS, t_lo);     \
+    else if (kind == 2) fwd_chunk<kBF16, true>(BUF, CH, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo); \
+    else fwd_chunk_zero(CH, ea, bprev, tS, t_lo);                                                \
+  }
 #pragma unroll 1
-      for (int ch = 0; ch < 8; ch += 2) {
-        tmem_ld16(tS + 16 * (ch + 1), bufB);
-        fwd_chunk<kBF16, true>(bufA, ch, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
-        tmem_ld_wait();
-        if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
-        fwd_chunk<kBF16, true>(bufB, ch + 1, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
-        tmem_ld_wait();
-      }
-    } else {
-#pragma unroll 1
-      for (int ch = 0; ch < 8; ch += 2) {
-        tmem_ld16(tS + 16 * (ch + 1), bufB);
-        fwd_chunk<kBF16, false>(bufA, ch, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
-        tmem_ld_wait();
-        if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
-        fwd_chunk<kBF16, false>(bufB, ch + 1, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo);
-        tmem_ld_wait();
-      }
+    for (int ch = 0; ch < 8; ch += 2) {
+      tmem_ld16(tS + 16 * (ch + 1), bufB);
+      CA_FWD_CHUNK(bufA, ch);
+      tmem_ld_wait();
+      if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
+      CA_FWD_CHUNK(bufB, ch + 1);
+      tmem_ld_wait();
     }
+#undef CA_FWD_CHUNK
     if (diag && i == j0 + BN - 1) {   // cap of key i sits in the last column: keep it pending
       bprev += 0.5f * ea;
       z += 0.5f * ea;
@@ -342,6 +422,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
       acc[d] = fmaf(bpend, vv, acc[d]);
     }
   }
+  z += z2.x + z2.y;
   const float inv = 1.f / z;
   uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + row * HD);
 #pragma unroll
@@ -653,6 +734,76 @@ __device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32
   }
 }
 
+// Interior version of bwd_keys8 (every key visible, no caps) in packed fp32
+// pairs.  Segment pairs (2x -> 2x+1, 2x+1 -> 2x+2) are the lanes: their left
+// keys (2x, 2x+1) form the natural register pairs of the raw TMEM rows, so s,
+// g and the exponent argument are computed packed there; each exponential goes
+// straight into the right-key pair (2x+1, 2x+2) where the moment recurrences use
+// it.  Products that mix the two layouts (differences, Ea * series, the final
+// L/R and A/B sums) are scalar.  The moments match seg_moments012_sel bit for
+// bit; L is formed as g_c A + G (M1 - M2).  ec carries e of key 0 between calls
+// (sc, gc are recomputed from the raw row); gsum2 collects scale * dS * s.
+template <bool kBF16>
+__device__ __forceinline__ void bwd_keys8_fast(const uint32_t (&sv)[16], const uint32_t (&pv)[16], int off,
+                                               uint32_t s_next, uint32_t p_next, float scale, float m2, float dds,
+                                               float& ec, float& Rprev, float& Bprev, float2& gsum2,
+                                               uint32_t (&pk)[4], uint32_t (&dk)[4]) {
+  const float2 scale2 = splat2(scale), l2e = splat2(kLog2e), nm2 = splat2(-m2), ndds = splat2(-dds);
+  const float2 neg1 = splat2(-1.f), neg2 = splat2(-2.f), half = splat2(0.5f);
+  float2 sA[4], gA[4];
+  float e[9];
+  e[0] = ec;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const float2 raw = make_float2(__uint_as_float(sv[(off + 2 * x) & 15]), __uint_as_float(sv[(off + 2 * x + 1) & 15]));
+    const float2 praw = make_float2(__uint_as_float(pv[(off + 2 * x) & 15]), __uint_as_float(pv[(off + 2 * x + 1) & 15]));
+    sA[x] = mul2(raw, scale2);
+    gA[x] = fma2(praw, scale2, ndds);
+    const float2 arg = fma2(sA[x], l2e, nm2);
+    if (x > 0) e[2 * x] = ex2_approx(arg.x);
+    e[2 * x + 1] = ex2_approx(arg.y);
+  }
+  const uint32_t s8_bits = (off + 8 < 16) ? sv[(off + 8) & 15] : s_next;
+  const uint32_t p8_bits = (off + 8 < 16) ? pv[(off + 8) & 15] : p_next;
+  const float s8 = __uint_as_float(s8_bits) * scale;
+  const float g8 = fmaf(__uint_as_float(p8_bits), scale, -dds);
+  e[8] = ex2_approx(fmaf(s8, kLog2e, -m2));
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const float sBy = (x < 3) ? sA[x + 1].x : s8;
+    const float gBy = (x < 3) ? gA[x + 1].x : g8;
+    const float2 EB = make_float2(e[2 * x + 1], e[2 * x + 2]);
+    const float2 d = make_float2(sA[x].y - sA[x].x, sBy - sA[x].y);
+    const float2 nd = mul2(d, neg1);
+    const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    const float2 m0c = mul2(make_float2(EB.x - e[2 * x], EB.y - e[2 * x + 1]), r);
+    const float2 m1c = mul2(fma2(m0c, neg1, EB), r);
+    const float2 m2c = mul2(fma2(m1c, neg2, EB), r);
+    float2 ser = fma2(splat2(1.f / 960.f), d, splat2(1.f / 168.f));
+    ser = fma2(ser, d, splat2(1.f / 36.f));
+    ser = fma2(ser, d, splat2(1.f / 10.f));
+    ser = fma2(ser, d, splat2(1.f / 4.f));
+    ser = fma2(ser, d, splat2(1.f / 3.f));
+    float2 M2;
+    M2.x = fabsf(d.x) < kSeriesMaxBwd ? e[2 * x] * ser.x : m2c.x;
+    M2.y = fabsf(d.y) < kSeriesMaxBwd ? e[2 * x + 1] * ser.y : m2c.y;
+    const float2 M1 = mul2(fma2(nd, M2, EB), half);
+    const float2 M0 = fma2(nd, M1, EB);
+    const float2 A = fma2(M1, neg1, M0);
+    const float2 G = make_float2(gA[x].y - gA[x].x, gBy - gA[x].y);
+    const float2 L = fma2(gA[x], A, mul2(G, fma2(M2, neg1, M1)));
+    const float2 R = fma2(gA[x], M1, mul2(G, M2));
+    const float ds0 = Rprev + L.x, ds1 = R.x + L.y;
+    const float p0 = Bprev + A.x, p1 = M1.x + A.y;
+    gsum2 = fma2(make_float2(ds0, ds1), sA[x], gsum2);
+    Rprev = R.y;
+    Bprev = M1.y;
+    pk[x] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+    dk[x] = kBF16 ? pack_bf16x2(ds0, ds1) : pack_f16x2(ds0, ds1);
+  }
+  ec = e[8];
+}
+
 // one 16-byte chunk (8 keys) of a query row; 128-byte swizzle: chunk ^ (row & 7)
 __device__ __forceinline__ void store_chunk(uint8_t* prow, uint8_t* drow, int chunk, int swz,
                                             const uint32_t (&pk)[4], const uint32_t (&dk)[4]) {
@@ -678,6 +829,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   uint8_t* const dbuf = sm.ds[qk >> 1];
   const int chunk0 = 4 * (qk & 1);         // first 16-byte chunk of this quarter in a 128-byte row
   float gsum = 0.f;
+  float2 gsum2 = splat2(0.f);   // packed partial of gsum from interior key groups
   bool ok = true;
 
   // row statistics of the next query tile are loaded one iteration ahead
@@ -702,11 +854,12 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
-    const int kbase = j0 + 32 * qk;              // key of local column 0
     const float m2 = row_ok ? fmaf(m, kLog2e, log2f(zrow)) : 0.f;   // E = e^{s-m} / Z
     const float dds = dd * scale;
-    // every key this thread touches is visible, inside [0, T) and capless: no masking needed
-    const bool interior = t >= 1 && kt >= 1 && (i0 + BM) <= Tn && (j0 + BN) < Tn;
+    // interior: every key this warp touches (kbase-1 .. kbase+32) is visible to all of
+    // its rows (i0+32rq .. i0+32rq+31), inside [0, T) and capless: no masking needed
+    const int kbase = j0 + 32 * qk;              // key of local column 0
+    const bool interior = kbase >= 1 && kbase + 32 <= i0 + 32 * rq && i0 + 32 * rq + 32 <= Tn;
     // chunk 0: left halo, keys 0..15, key 16
     uint32_t s_lo, p_lo, s16, p16, sv[16], pv[16];
     tmem_ld1(colS - 1, s_lo);
@@ -740,17 +893,18 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     uint32_t pk[4], dk[4];
 #define CA_KEYS8(EDGE, OFF, SN, PN, KF)                                                                   \
   bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Rprev, Bprev, gsum, pk, dk)
+#define CA_KEYS8_ANY(OFF, SN, PN, KF)                                                                     \
+  if (interior) bwd_keys8_fast<kBF16>(sv, pv, OFF, SN, PN, scale, m2, dds, ec, Rprev, Bprev, gsum2, pk, dk); \
+  else CA_KEYS8(true, OFF, SN, PN, KF);
     // keys 0..7 are computed before waiting for the previous tile's dV/dK/dQ products,
     // which still read the shared P/dS buffer; their latency hides behind this work
-    if (interior) CA_KEYS8(false, 0, s16, p16, kbase);
-    else CA_KEYS8(true, 0, s16, p16, kbase);
+    CA_KEYS8_ANY(0, s16, p16, kbase);
     if (t > 0) {
       const bool got2 = mbar_wait(&sm.bar_mma_done, (t - 1) & 1, ab);
       if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
     }
     store_chunk(prow, drow, chunk0, swz, pk, dk);
-    if (interior) CA_KEYS8(false, 8, s16, p16, kbase + 8);
-    else CA_KEYS8(true, 8, s16, p16, kbase + 8);
+    CA_KEYS8_ANY(8, s16, p16, kbase + 8);
     store_chunk(prow, drow, chunk0 + 1, swz, pk, dk);
     // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
     uint32_t s_hi, p_hi;
@@ -761,12 +915,11 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     tmem_ld_wait();
     tc_fence_before();
     mbar_arrive(&sm.bar_s_consumed);
-    if (interior) CA_KEYS8(false, 0, s_hi, p_hi, kbase + 16);
-    else CA_KEYS8(true, 0, s_hi, p_hi, kbase + 16);
+    CA_KEYS8_ANY(0, s_hi, p_hi, kbase + 16);
     store_chunk(prow, drow, chunk0 + 2, swz, pk, dk);
-    if (interior) CA_KEYS8(false, 8, s_hi, p_hi, kbase + 24);
-    else CA_KEYS8(true, 8, s_hi, p_hi, kbase + 24);
+    CA_KEYS8_ANY(8, s_hi, p_hi, kbase + 24);
     store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
+#undef CA_KEYS8_ANY
 #undef CA_KEYS8
     // dQ of the previous query tile: TMEM -> fp32 accumulator in global memory
     if (t > 0) {
@@ -828,7 +981,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     }
   }
   // d log_gain partial of this key tile: sum over the CTA of dS * s (gsum holds scale * that)
-  gsum /= scale;
+  gsum = (gsum + (gsum2.x + gsum2.y)) / scale;
   for (int off = 16; off > 0; off >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, off);
   if (lane == 0) sm.red[warp] = gsum;
   named_bar_sync(1, NUM_MATH_WARPS * 32);
