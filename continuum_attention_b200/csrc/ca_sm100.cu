@@ -321,7 +321,6 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     const int j0 = j * BN;
     const bool diag = (j == n_tiles - 1);
     const int nvis = diag ? min(i - j0 + 1, BN) : BN;
-    const bool edge = diag || j == 0;
     // pass 1: tile max over the visible keys
     uint32_t sr[2][32];
     float tmax = -INFINITY;
@@ -520,7 +519,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 //     into a 128-byte-swizzled shared buffer [2 key halves][128 queries][64 keys].
 //     The same bytes are the MN-major A operand of dV / dK (M = keys) and the
 //     K-major A operand of dQ (M = queries).  dQ of the previous query tile is
-//     read from TMEM and added to the fp32 dQ accumulator with red.global.add.
+//     read from TMEM into a swizzled f32 staging tile; the producer adds it to
+//     the global fp32 dQ accumulator with two TMA reduce-adds (32 columns each),
+//     so the adds travel as whole 128-byte rows instead of per-thread atomics.
 // Replaces cuda/continuum_attention.py:713-764 (recompute, dW = dY V^T, the
 // analytic score VJP kernels :192-293/:337-405, and the dV/dQ/dK GEMMs).
 namespace bwd {
@@ -532,7 +533,7 @@ constexpr int KH = 160;              // staged key rows: j0-16 .. j0+143
 constexpr int KOFF = 16;             // TMEM / SMEM row of key j0
 constexpr int NUM_MATH_WARPS = 16;
 constexpr int NUM_THREADS = (NUM_MATH_WARPS + 1) * 32;
-constexpr int QSTAGES = 3;
+constexpr int QSTAGES = 2;
 constexpr uint32_t KV_BYTES = KH * HD * 2;      // 20 KB
 constexpr uint32_t QT_BYTES = BM * HD * 2;      // 16 KB
 constexpr uint32_t HALF_BYTES = BM * 128;       // 16 KB: 128 query rows x 64 keys bf16
@@ -546,6 +547,7 @@ struct __align__(1024) Smem {
   uint8_t dout[QSTAGES][QT_BYTES];
   uint8_t p[2][HALF_BYTES];          // P   (bf16), [key half][query row][64 keys], swizzled
   uint8_t ds[2][HALF_BYTES];         // scale * dS (bf16), same layout
+  uint8_t dqs[2][HALF_BYTES];        // dQ of one query tile (f32): [32-column half][row][128 B], swizzled
   uint64_t bar_kv;
   uint64_t bar_qdo[QSTAGES];
   uint64_t bar_s_full;
@@ -553,6 +555,7 @@ struct __align__(1024) Smem {
   uint64_t bar_p_ready;
   uint64_t bar_mma_done;
   uint64_t bar_drain;
+  uint64_t bar_dq_free;              // the staged dQ tile has been read by its reduce
   uint32_t tmem_base;
   int abort_flag;
   float red[NUM_MATH_WARPS];
@@ -603,14 +606,19 @@ __device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tme
 
 template <bool kBF16>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
-                         const CUtensorMap* tdo, int bh, int j0, int n_tiles, uint32_t tmem) {
+                         const CUtensorMap* tdo, const CUtensorMap* tdq, int bh, int j0, int n_tiles,
+                         uint32_t tmem) {
   volatile int* ab = &sm.abort_flag;
   const uint32_t id_s = make_idesc(BM, KH, kBF16, false, false);
   const uint32_t id_mn = make_idesc(BN, HD, kBF16, true, true);
   const uint32_t id_dq = make_idesc(BM, HD, kBF16, true, false);
   bool kv_pending = true;
-  bool q_pending[QSTAGES] = {false, false, false};
-  uint32_t q_phase[QSTAGES] = {0, 0, 0};
+  bool q_pending[QSTAGES];
+  uint32_t q_phase[QSTAGES];
+  for (int s2 = 0; s2 < QSTAGES; ++s2) {
+    q_pending[s2] = false;
+    q_phase[s2] = 0;
+  }
 
   mbar_arrive_expect_tx(&sm.bar_kv, 2 * KV_BYTES);
   tma_load_3d(sm.k, tk, &sm.bar_kv, 0, j0 - KOFF, bh);
@@ -644,6 +652,12 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
       tc_fence_after();
       issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
       mma_commit(&sm.bar_mma_done);
+      // the math warps staged dQ of query tile t-1 before arriving on p_ready
+      if (t > 0) {
+        tma_reduce_add_3d(tdq, sm.dqs[0], 0, j0 + (t - 1) * BM, bh);
+        tma_reduce_add_3d(tdq, sm.dqs[1], 32, j0 + (t - 1) * BM, bh);
+        bulk_commit_group();
+      }
       if (t + QSTAGES < n_tiles) {
         if (!mbar_wait(&sm.bar_mma_done, t & 1, ab)) break;
         const int tt = t + QSTAGES;
@@ -651,6 +665,18 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
         tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
         q_pending[st] = true;
+      }
+      if (t > 0) {
+        bulk_wait_group_read0();
+        mbar_arrive(&sm.bar_dq_free);
+      }
+      if (t == n_tiles - 1) {
+        // the last tile's dQ is staged after the loop (p_ready phase n_tiles)
+        if (mbar_wait(&sm.bar_p_ready, n_tiles & 1, ab)) {
+          tma_reduce_add_3d(tdq, sm.dqs[0], 0, j0 + t * BM, bh);
+          tma_reduce_add_3d(tdq, sm.dqs[1], 32, j0 + t * BM, bh);
+          bulk_commit_group();
+        }
       }
     }
   }
@@ -662,6 +688,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   for (int s2 = 0; s2 < QSTAGES; ++s2)
     if (q_pending[s2]) mbar_wait(&sm.bar_qdo[s2], q_phase[s2], nab);
   mbar_wait(&sm.bar_drain, 0, nab);
+  bulk_wait_group0();   // dQ reduces complete (shared source read, global adds done)
 }
 
 // scale*dS and P for 8 consecutive keys of one query row, packed as 16-bit pairs.
@@ -812,9 +839,22 @@ __device__ __forceinline__ void store_chunk(uint8_t* prow, uint8_t* drow, int ch
   *reinterpret_cast<uint4*>(drow + off) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
 }
 
+// One thread's 16 dQ columns (16qk .. 16qk+15) of query row r into the staging
+// tile: half qk/2 holds columns 32(qk/2) .. +31 as 128-byte rows with the TMA
+// 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)).
+__device__ __forceinline__ void stage_dq(Smem& sm, int r, int qk, const uint32_t (&qv)[16]) {
+  uint8_t* const row = sm.dqs[qk >> 1] + (uint32_t)r * 128;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int chunk = 4 * (qk & 1) + x;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (r & 7)) << 4)) =
+        make_uint4(qv[4 * x], qv[4 * x + 1], qv[4 * x + 2], qv[4 * x + 3]);
+  }
+}
+
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
-                           float* dq_acc, void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
+                           void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
                            int kt, int nkt, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -921,40 +961,39 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
 #undef CA_KEYS8_ANY
 #undef CA_KEYS8
-    // dQ of the previous query tile: TMEM -> fp32 accumulator in global memory
+    // dQ of the previous query tile: TMEM -> swizzled f32 staging tile, which the
+    // producer adds into the global accumulator with two TMA reduces once every
+    // warp has arrived on p_ready.  The staging tile is free once the reduce of
+    // tile t-2 has read it.
     if (t > 0) {
+      if (t > 1) {
+        const bool got3 = mbar_wait(&sm.bar_dq_free, t & 1, ab);
+        if (!__all_sync(0xffffffffu, got3)) { ok = false; break; }
+      }
       uint32_t qv[16];
       tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
       tmem_ld_wait();
-      const int ip = i0 - BM + r;
-      if (ip < Tn) {
-        float* dst = dq_acc + ((size_t)bh * Tn + ip) * HD + 16 * qk;
-#pragma unroll
-        for (int x = 0; x < 16; x += 4)
-          red_add_v4(dst + x, __uint_as_float(qv[x]), __uint_as_float(qv[x + 1]), __uint_as_float(qv[x + 2]),
-                     __uint_as_float(qv[x + 3]));
-      }
+      stage_dq(sm, r, qk, qv);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(&sm.bar_p_ready);
   }
 
-  // last dQ tile and the dK / dV accumulators
+  // last dQ tile (staged for the producer's final reduce) and the dK / dV accumulators
   if (ok) ok = mbar_wait(&sm.bar_mma_done, (n_tiles - 1) & 1, ab);
   ok = __all_sync(0xffffffffu, ok);
   tc_fence_after();
-  {
+  if (ok) {
+    if (n_tiles > 1) ok = mbar_wait(&sm.bar_dq_free, n_tiles & 1, ab);
+    ok = __all_sync(0xffffffffu, ok);
     uint32_t qv[16];
     tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
     tmem_ld_wait();
-    const int ip = j0 + (n_tiles - 1) * BM + r;
-    if (ok && ip < Tn) {
-      float* dst = dq_acc + ((size_t)bh * Tn + ip) * HD + 16 * qk;
-#pragma unroll
-      for (int x = 0; x < 16; x += 4)
-        red_add_v4(dst + x, __uint_as_float(qv[x]), __uint_as_float(qv[x + 1]), __uint_as_float(qv[x + 2]),
-                   __uint_as_float(qv[x + 3]));
+    if (ok) {
+      stage_dq(sm, r, qk, qv);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.bar_p_ready);
     }
   }
   {
@@ -996,8 +1035,9 @@ template <bool kBF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-           const float* __restrict__ log_gain, const float* __restrict__ stats, const float* __restrict__ rowdot,
-           float* __restrict__ dq_acc, void* __restrict__ dkp, void* __restrict__ dvp,
+           const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ log_gain,
+           const float* __restrict__ stats, const float* __restrict__ rowdot,
+           void* __restrict__ dkp, void* __restrict__ dvp,
            float* __restrict__ gain_part, int BH, int H, int Tn, float inv_sqrt_d) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1017,12 +1057,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       mbar_init(&sm.bar_p_ready, NUM_MATH_WARPS * 32);
       mbar_init(&sm.bar_mma_done, 1);
       mbar_init(&sm.bar_drain, 1);
+      mbar_init(&sm.bar_dq_free, 1);
       sm.abort_flag = 0;
       fence_mbar_init();
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
+      tma_prefetch_desc(&tm_dq);
     }
     __syncwarp();
     tmem_alloc(&sm.tmem_base, TMEM_COLS);
@@ -1034,10 +1076,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == NUM_MATH_WARPS) {
-    if (lane == 0) producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, bh, j0, n_tiles, tmem);
+    if (lane == 0) producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, bh, j0, n_tiles, tmem);
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, log_gain, stats, rowdot, dq_acc, dkp, dvp, gain_part, bh, bh % H, Tn, j0, kt, nkt,
+    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, bh, bh % H, Tn, j0, kt, nkt,
                       n_tiles, tmem, inv_sqrt_d);
   }
   tc_fence_before();
@@ -1084,6 +1126,20 @@ static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T
   return r == CUDA_SUCCESS;
 }
 
+// [BH, T, 64] f32 accumulator, box = {32, 128, 1} (128-byte rows), 128-byte swizzle
+static bool make_map_f32(CUtensorMap* m, void* base, long long BH, long long T) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)T, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {64 * 4, (cuuint64_t)(T * 64 * 4)};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool forward_supported(const FwdArgs& a) {
@@ -1118,9 +1174,10 @@ cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a
 template <bool kBF16>
 static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   const long long BH = a.B * a.H;
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
   if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM) ||
-      !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH))
+      !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH) ||
+      !make_map_f32(&mdq, w.dq_acc, BH, a.T))
     return cudaErrorInvalidValue;
   cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc);
   if (e != cudaSuccess) return e;
@@ -1129,7 +1186,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   if (e != cudaSuccess) return e;
   const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;
   kern<<<dim3((unsigned)(BH * nkt)), bwd::NUM_THREADS, bwd::kSmemBytes, a.stream>>>(
-      mq, mk, mv, mdo, a.log_gain, a.row_stats, w.rowdot, w.dq_acc, a.dk, a.dv,
+      mq, mk, mv, mdo, mdq, a.log_gain, a.row_stats, w.rowdot, a.dk, a.dv,
       a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
