@@ -5,7 +5,9 @@
 //   warp 4 (one elected lane) is the producer: TMA loads of Q (once) and of
 //     K/V tiles into a 2-stage ring, and the tcgen05.mma issue:
 //       S(j)  = Q K_j^T              128x128 fp32 in TMEM columns [0,128)
-//       O    += P_hi(j) V'_j + P_lo(j) V'_j   128x64 fp32 in TMEM columns [128,192)
+//       O    += P_hi(j) V'_j + P_lo(j) V'_j   128x64 fp32 in TMEM columns [128,192),
+//               issued in two halves of 64 keys: the first as soon as the math
+//               warps have written P for keys 0..63, overlapping the second half
 //     where V'_j is the V tile staged one row early (keys j0-1 .. j0+126) and
 //     P(j) is written by the math warps over the same TMEM columns as S(j).
 //   warps 0-3 (thread = query row = TMEM lane) load their S row, keep an online
@@ -55,7 +57,8 @@ struct __align__(1024) Smem {
   uint64_t bar_v[STAGES];
   uint64_t bar_kv_free[STAGES];
   uint64_t bar_s_full;
-  uint64_t bar_p_ready;
+  uint64_t bar_p_half;               // P of keys 0..63 of the tile is in TMEM
+  uint64_t bar_p_ready;              // all of P is in TMEM
   uint64_t bar_o_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -72,12 +75,14 @@ __device__ __forceinline__ void issue_s(uint32_t q_saddr, uint32_t k_saddr, uint
   }
 }
 
-__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, uint32_t idesc,
-                                         bool accumulate) {
+// O += P V' over keys 64h .. 64h+63 of the tile (h = 0, 1), hi and lo parts.
+__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, uint32_t idesc,
+                                              int h, bool accumulate) {
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
 #pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) {
+    for (int k4 = 0; k4 < BN / 32; ++k4) {
+      const int kk = 4 * h + k4;
       const uint64_t b = sdesc_sw128(v_saddr + kk * 2048, 16384, 1024);   // V: MN-major
       const uint32_t acc = (accumulate || part > 0 || kk > 0) ? 1u : 0u;
       mma_ts(o_tmem, p_tmem + (part ? TMEM_PLO : TMEM_S) + kk * 8, b, idesc, acc);
@@ -118,12 +123,16 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     mma_issued = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j % STAGES;
-      if (!mbar_wait(&sm.bar_p_ready, j & 1, ab)) break;
+      // the first half of P V' runs while the math warps form the second half of P
+      if (!mbar_wait(&sm.bar_p_half, j & 1, ab)) break;
       if (!mbar_wait(&sm.bar_v[st], v_phase[st], ab)) break;
       v_pending[st] = false;
       v_phase[st] ^= 1;
       tc_fence_after();
-      issue_pv(o_tmem, tmem, smem_u32(sm.v[st]), id_o, j > 0);
+      issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 0, j > 0);
+      if (!mbar_wait(&sm.bar_p_ready, j & 1, ab)) break;
+      tc_fence_after();
+      issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 1, true);
       mma_commit(&sm.bar_kv_free[st]);
       if (j + 1 < n_tiles) {
         const int st1 = (j + 1) % STAGES;
@@ -239,8 +248,7 @@ __device__ __forceinline__ void fwd_chunk_fast(const uint32_t (&cur)[16], int ch
     const float2 rn = make_float2(rcp_approx(nd.x), rcp_approx(nd.y));
     const float2 m0c = mul2(make_float2(ea - eb.x, eb.x - eb.y), rn);
     const float2 m1c = mul2(fma2(eb, neg1, m0c), rn);
-    float2 ps = fma2(splat2(1.f / 144.f), nd, splat2(-1.f / 30.f));
-    ps = fma2(ps, nd, splat2(1.f / 8.f));
+    float2 ps = fma2(splat2(-1.f / 30.f), nd, splat2(1.f / 8.f));
     ps = fma2(ps, nd, splat2(-1.f / 3.f));
     ps = fma2(ps, nd, splat2(1.f / 2.f));
     float2 M1;
@@ -386,6 +394,11 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
       if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
       CA_FWD_CHUNK(bufB, ch + 1);
       tmem_ld_wait();
+      if (ch == 2) {   // P of keys 0..63 complete: the producer starts its half of P V'
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.bar_p_half);
+      }
     }
 #undef CA_FWD_CHUNK
     if (diag && i == j0 + BN - 1) {   // cap of key i sits in the last column: keep it pending
@@ -468,6 +481,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         mbar_init(&sm.bar_kv_free[s], 1);
       }
       mbar_init(&sm.bar_s_full, 1);
+      mbar_init(&sm.bar_p_half, 128);
       mbar_init(&sm.bar_p_ready, 128);
       mbar_init(&sm.bar_o_done, 1);
       sm.abort_flag = 0;
@@ -806,9 +820,7 @@ __device__ __forceinline__ void bwd_keys8_fast(const uint32_t (&sv)[16], const u
     const float2 m0c = mul2(make_float2(EB.x - e[2 * x], EB.y - e[2 * x + 1]), r);
     const float2 m1c = mul2(fma2(m0c, neg1, EB), r);
     const float2 m2c = mul2(fma2(m1c, neg2, EB), r);
-    float2 ser = fma2(splat2(1.f / 960.f), d, splat2(1.f / 168.f));
-    ser = fma2(ser, d, splat2(1.f / 36.f));
-    ser = fma2(ser, d, splat2(1.f / 10.f));
+    float2 ser = fma2(splat2(1.f / 36.f), d, splat2(1.f / 10.f));
     ser = fma2(ser, d, splat2(1.f / 4.f));
     ser = fma2(ser, d, splat2(1.f / 3.f));
     float2 M2;
@@ -894,7 +906,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
-    const float m2 = row_ok ? fmaf(m, kLog2e, log2f(zrow)) : 0.f;   // E = e^{s-m} / Z
+    const float m2 = row_ok ? fmaf(m, kLog2e, lg2_approx(zrow)) : 0.f;   // E = e^{s-m} / Z
     const float dds = dd * scale;
     // interior: every key this warp touches (kbase-1 .. kbase+32) is visible to all of
     // its rows (i0+32rq .. i0+32rq+31), inside [0, T) and capless: no masking needed
