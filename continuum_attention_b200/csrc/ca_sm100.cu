@@ -2,7 +2,8 @@
 // head dim 64): TMA-staged Q/K/V tiles, tcgen05.mma with TMEM accumulators.
 //
 // Forward, one CTA per 128-row query tile (two CTAs per SM):
-//   warp 4 (one elected lane) is the producer: TMA loads of Q (once) and of
+//   warp 4 is the producer (the whole warp runs converged; lane 0 issues): TMA
+//     loads of Q (once) and of
 //     K/V tiles into a 2-stage ring, and the tcgen05.mma issue:
 //       S(j)  = Q K_j^T              128x128 fp32 in TMEM columns [0,128)
 //       O    += P_hi(j) V'_j + P_lo(j) V'_j   128x64 fp32 in TMEM columns [128,192),
@@ -113,7 +114,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   const uint32_t q_sa = smem_u32(sm.q);
   const uint32_t s_tmem = tmem + TMEM_S, o_tmem = tmem + TMEM_O;
 
-  if (mbar_wait(&sm.bar_q, 0, ab) && mbar_wait(&sm.bar_k[0], 0, ab)) {
+  if (mbar_wait_warp(&sm.bar_q, 0, ab) && mbar_wait_warp(&sm.bar_k[0], 0, ab)) {
     q_pending = false;
     k_pending[0] = false;
     k_phase[0] ^= 1;
@@ -124,19 +125,19 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j % STAGES;
       // the first half of P V' runs while the math warps form the second half of P
-      if (!mbar_wait(&sm.bar_p_half, j & 1, ab)) break;
-      if (!mbar_wait(&sm.bar_v[st], v_phase[st], ab)) break;
+      if (!mbar_wait_warp(&sm.bar_p_half, j & 1, ab)) break;
+      if (!mbar_wait_warp(&sm.bar_v[st], v_phase[st], ab)) break;
       v_pending[st] = false;
       v_phase[st] ^= 1;
       tc_fence_after();
       issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 0, j > 0);
-      if (!mbar_wait(&sm.bar_p_ready, j & 1, ab)) break;
+      if (!mbar_wait_warp(&sm.bar_p_ready, j & 1, ab)) break;
       tc_fence_after();
       issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 1, true);
       mma_commit(&sm.bar_kv_free[st]);
       if (j + 1 < n_tiles) {
         const int st1 = (j + 1) % STAGES;
-        if (!mbar_wait(&sm.bar_k[st1], k_phase[st1], ab)) break;
+        if (!mbar_wait_warp(&sm.bar_k[st1], k_phase[st1], ab)) break;
         k_pending[st1] = false;
         k_phase[st1] ^= 1;
         tc_fence_after();
@@ -145,7 +146,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
       }
       if (j + STAGES < n_tiles) {
         // stage st is free once S(j) and PV(j) have consumed it
-        if (!mbar_wait(&sm.bar_kv_free[st], (j / STAGES) & 1, ab)) break;
+        if (!mbar_wait_warp(&sm.bar_kv_free[st], (j / STAGES) & 1, ab)) break;
         const int t = j + STAGES;
         mbar_arrive_expect_tx(&sm.bar_k[st], TILE_BYTES);
         tma_load_3d(sm.k[st], tk, &sm.bar_k[st], 0, t * BN, bh);
@@ -160,13 +161,13 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   // drain: in-flight TMA copies must land before the CTA's shared memory goes away
   int dummy_abort = 0;
   volatile int* nab = &dummy_abort;
-  if (q_pending) mbar_wait(&sm.bar_q, 0, nab);
+  if (q_pending) mbar_wait_warp(&sm.bar_q, 0, nab);
   for (int s = 0; s < STAGES; ++s) {
-    if (k_pending[s]) mbar_wait(&sm.bar_k[s], k_phase[s], nab);
-    if (v_pending[s]) mbar_wait(&sm.bar_v[s], v_phase[s], nab);
+    if (k_pending[s]) mbar_wait_warp(&sm.bar_k[s], k_phase[s], nab);
+    if (v_pending[s]) mbar_wait_warp(&sm.bar_v[s], v_phase[s], nab);
   }
   (void)mma_issued;
-  mbar_wait(&sm.bar_o_done, 0, nab);
+  mbar_wait_warp(&sm.bar_o_done, 0, nab);
 }
 
 // P for 16 keys of one row: keys j0-1+c for c = 16*ch .. 16*ch+15 (P column c).
@@ -500,7 +501,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 4) {
-    if (lane == 0) producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, n_tiles, tmem);
+    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, n_tiles, tmem);   // whole warp, converged
     __syncwarp();
   } else {
     math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, n_tiles, tmem, inv_sqrt_d);
@@ -518,7 +519,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 // ---------------------------------------------------------------------------
 // Backward, one CTA per 128-key tile [j0, j0+128), looping over the query
 // tiles i0 = j0, j0+128, ... (one CTA per SM):
-//   warp 16 (one elected lane) is the producer:
+//   warp 16 is the producer (the whole warp runs converged; lane 0 issues):
 //     TMA: K' and V' (keys j0-16 .. j0+143, stationary), Q and dO tiles (2 stages)
 //     S  = Q K'^T   128x160 fp32, TMEM columns [0,160)    (key j0+x at column 16+x)
 //     dP = dO V'^T  128x160 fp32, TMEM columns [160,320)
@@ -643,7 +644,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     tma_load_3d(sm.dout[t], tdo, &sm.bar_qdo[t], 0, j0 + t * BM, bh);
     q_pending[t] = true;
   }
-  if (mbar_wait(&sm.bar_kv, 0, ab) && mbar_wait(&sm.bar_qdo[0], 0, ab)) {
+  if (mbar_wait_warp(&sm.bar_kv, 0, ab) && mbar_wait_warp(&sm.bar_qdo[0], 0, ab)) {
     kv_pending = false;
     q_pending[0] = false;
     q_phase[0] ^= 1;
@@ -652,17 +653,17 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     mma_commit(&sm.bar_s_full);
     for (int t = 0; t < n_tiles; ++t) {
       const int st = t % QSTAGES;
-      if (!mbar_wait(&sm.bar_s_consumed, t & 1, ab)) break;
+      if (!mbar_wait_warp(&sm.bar_s_consumed, t & 1, ab)) break;
       if (t + 1 < n_tiles) {
         const int st1 = (t + 1) % QSTAGES;
-        if (!mbar_wait(&sm.bar_qdo[st1], q_phase[st1], ab)) break;
+        if (!mbar_wait_warp(&sm.bar_qdo[st1], q_phase[st1], ab)) break;
         q_pending[st1] = false;
         q_phase[st1] ^= 1;
         tc_fence_after();
         issue_s_dp<kBF16>(sm, st1, tmem, id_s);
         mma_commit(&sm.bar_s_full);
       }
-      if (!mbar_wait(&sm.bar_p_ready, t & 1, ab)) break;
+      if (!mbar_wait_warp(&sm.bar_p_ready, t & 1, ab)) break;
       tc_fence_after();
       issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
       mma_commit(&sm.bar_mma_done);
@@ -673,7 +674,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         bulk_commit_group();
       }
       if (t + QSTAGES < n_tiles) {
-        if (!mbar_wait(&sm.bar_mma_done, t & 1, ab)) break;
+        if (!mbar_wait_warp(&sm.bar_mma_done, t & 1, ab)) break;
         const int tt = t + QSTAGES;
         mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
         tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
@@ -682,11 +683,12 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
       }
       if (t > 0) {
         bulk_wait_group_read0();
-        mbar_arrive(&sm.bar_dq_free);
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.bar_dq_free);
+        __syncwarp();
       }
       if (t == n_tiles - 1) {
         // the last tile's dQ is staged after the loop (p_ready phase n_tiles)
-        if (mbar_wait(&sm.bar_p_ready, n_tiles & 1, ab)) {
+        if (mbar_wait_warp(&sm.bar_p_ready, n_tiles & 1, ab)) {
           tma_reduce_add_3d(tdq, sm.dqs[0], 0, j0 + t * BM, bh);
           tma_reduce_add_3d(tdq, sm.dqs[1], 32, j0 + t * BM, bh);
           bulk_commit_group();
@@ -698,10 +700,10 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   mma_commit(&sm.bar_drain);
   int dummy = 0;
   volatile int* nab = &dummy;
-  if (kv_pending) mbar_wait(&sm.bar_kv, 0, nab);
+  if (kv_pending) mbar_wait_warp(&sm.bar_kv, 0, nab);
   for (int s2 = 0; s2 < QSTAGES; ++s2)
-    if (q_pending[s2]) mbar_wait(&sm.bar_qdo[s2], q_phase[s2], nab);
-  mbar_wait(&sm.bar_drain, 0, nab);
+    if (q_pending[s2]) mbar_wait_warp(&sm.bar_qdo[s2], q_phase[s2], nab);
+  mbar_wait_warp(&sm.bar_drain, 0, nab);
   bulk_wait_group0();   // dQ reduces complete (shared source read, global adds done)
 }
 
@@ -1088,7 +1090,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == NUM_MATH_WARPS) {
-    if (lane == 0) producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, bh, j0, n_tiles, tmem);
+    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, bh, j0, n_tiles, tmem);   // whole warp, converged
     __syncwarp();
   } else {
     math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, bh, bh % H, Tn, j0, kt, nkt,

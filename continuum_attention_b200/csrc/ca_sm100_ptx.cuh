@@ -44,8 +44,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// The issue helpers marked "lane 0" below (expect_tx arrival, TMA copies, MMAs,
+// commits) act only in lane 0 of the calling warp: a producer warp runs its
+// whole loop converged, so descriptors and addresses stay warp-uniform, and the
+// single issuing lane is selected by a predicate inside the instruction.
+#define CA_LANE0_PRED ".reg .pred l0;\n\t.reg .u32 lid;\n\tmov.u32 lid, %%laneid;\n\tsetp.eq.u32 l0, lid, 0;\n\t"
+
+// lane 0
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+  asm volatile("{\n\t" CA_LANE0_PRED "@l0 mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
                : "memory");
 }
 
@@ -63,6 +72,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase with the given parity.  Gives up after kWaitLimitNs,
 // records CA_ERR_DEVICE_TIMEOUT in g_device_status and sets *abort_flag.
+// Any number of threads may wait on the same barrier.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
@@ -77,16 +87,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait by a whole converged warp, with one answer for every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 3-D tiled load (no multicast) completing on an mbarrier transaction count.
+// 3-D tiled load (no multicast) completing on an mbarrier transaction count.  Lane 0.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+      "{\n\t" CA_LANE0_PRED
+      "@l0 cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n\t}" ::"r"(
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
@@ -94,15 +111,20 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 
 // 3-D tiled reduce-add of a shared-memory box into global memory (element type of
 // the tensor map, here f32), tracked by the issuing thread's bulk async-groups.
-// Rows outside the tensor are skipped.
+// Rows outside the tensor are skipped.  Lane 0 (as is bulk_commit_group; the
+// waits may run in every lane: the other lanes have no groups to wait for).
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
   asm volatile(
-      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+      "{\n\t" CA_LANE0_PRED
+      "@l0 cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];\n\t}" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_commit_group() {
+  // (the unused operand makes this an operand-carrying asm, so %% is unescaped as elsewhere)
+  asm volatile("{\n\t" CA_LANE0_PRED "@l0 cp.async.bulk.commit_group;\n\t}" ::"n"(0) : "memory");
+}
 // the shared-memory sources of every committed group have been read
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -218,31 +240,33 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
-// D[tmem] (+)= A[smem] * B[smem]
+// D[tmem] (+)= A[smem] * B[smem].  Lane 0.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p;\n\t" CA_LANE0_PRED
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@l0 tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]   (A: lane = row, 2 x 16-bit K elements per column)
+// D[tmem] (+)= A[tmem] * B[smem]   (A: lane = row, 2 x 16-bit K elements per column).  Lane 0.
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p;\n\t" CA_LANE0_PRED
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@l0 tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrive on an mbarrier once every tcgen05 operation this thread issued so far completes.
+// Arrive on an mbarrier once every tcgen05 operation this thread issued so far completes.  Lane 0.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+  asm volatile("{\n\t" CA_LANE0_PRED
+               "@l0 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+                   smem_u32(bar))
                : "memory");
 }
 
