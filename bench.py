@@ -271,37 +271,40 @@ def run_ours(args, world, rank, local):
     ws = torch.empty(ca.workspace_bytes(B, H, T, D, dtype), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(i, ev=None):
+    def step(i, ev_mid=None, ev_end=None):
         q, k, v, dy = sets[i % N_INPUT_SETS]
-        if ev is not None:
-            ev[0].record(stream)
         o, stats, o32 = ca.forward_raw(q, k, v, lg, impl=impl, want_f32=True)
         nf = _native.lib().ca_last_launch_count()
-        if ev is not None:
-            ev[1].record(stream)
+        if ev_mid is not None:
+            ev_mid.record(stream)
         ca.backward_raw(q, k, v, o, dy, lg, stats, want_dgain=True, impl=impl, workspace=ws, o_f32=o32)
         nb = _native.lib().ca_last_launch_count()
-        if ev is not None:
-            ev[2].record(stream)
+        if ev_end is not None:
+            ev_end.record(stream)
         return nf + nb
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    # two events per step: after the forward call and after the backward call; the
+    # forward of step i runs between the end of step i-1 (or the start) and mid_i
+    ev_start = torch.cuda.Event(enable_timing=True)
+    ev_mid = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches = 0
     with ClockSampler(local) as clk:
         time.sleep(0.25)
         _barrier(world)
         torch.cuda.synchronize()
+        ev_start.record(stream)
         for i in range(args.steps):
-            launches += step(args.warmup + i, evs[i])
+            launches += step(args.warmup + i, ev_mid[i], ev_end[i])
         torch.cuda.synchronize()
         _barrier(world)
         time.sleep(0.1)
-    total_ms = evs[0][0].elapsed_time(evs[-1][2])
-    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    total_ms = ev_start.elapsed_time(ev_end[-1])
+    fwd_ms = [(ev_start if i == 0 else ev_end[i - 1]).elapsed_time(ev_mid[i]) for i in range(args.steps)]
+    bwd_ms = [ev_mid[i].elapsed_time(ev_end[i]) for i in range(args.steps)]
     total_ms = _max_over_ranks(world, total_ms)
     ms_step = total_ms / args.steps
     value = world * flops_per_step() * args.steps / (total_ms * 1e-3) / 1e12
