@@ -14,7 +14,8 @@ Metric: CA fwd+bwd TFLOP/s counting the two GEMMs per direction,
 4*B*H*T^2*D per step (3.436e10 at config 2).  ``value`` is device-timed
 (CUDA events, max over ranks) with inputs resident in HBM; ``e2e`` is the same
 metric through the public autograd op with pinned host inputs copied in and
-gradients copied out inside the timed region.
+gradients copied out inside the timed region, consecutive steps pipelined over
+a copy-in, a compute and a copy-out stream.
 
 The line also carries "decoder": the CA-S decoder training step (BASELINE
 config 4, 101,205,120 parameters, 8 x 2048 random bytes per GPU, bf16 autocast,
@@ -309,24 +310,51 @@ def run_ours(args, world, rank, local):
     ms_step = total_ms / args.steps
     value = world * flops_per_step() * args.steps / (total_ms * 1e-3) / 1e12
 
-    # end to end: public autograd op, pinned host buffers, copies inside the timed region
+    # end to end: public autograd op, pinned host buffers, copies inside the timed region.
+    # Three streams pipeline consecutive steps: step i's host->device copies (s_in)
+    # overlap step i-1's compute, and its device->host copies (s_out) overlap step
+    # i+1's; input and host-output buffers are double-buffered.  Every step still
+    # moves its own inputs in and its own gradients out inside the timed region.
     host = [tuple(t.cpu().pin_memory() for t in sets[j]) for j in range(2)]
-    outs = [torch.empty(SHAPE, dtype=dtype).pin_memory() for _ in range(3)]
-    gout = torch.empty(H, dtype=torch.float32).pin_memory()
+    outs = [[torch.empty(SHAPE, dtype=dtype).pin_memory() for _ in range(3)] +
+            [torch.empty(H, dtype=torch.float32).pin_memory()] for _ in range(2)]
+    dev_in = [[torch.empty(SHAPE, dtype=dtype, device=dev) for _ in range(4)] for _ in range(2)]
     lg_req = torch.zeros(H, device=dev, requires_grad=True)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    in_used = [False, False]
+    held = []   # (gradients, copy-out event) of the steps whose copies may still run
 
     def e2e_step(i):
-        hq, hk, hv, hdy = host[i % 2]
-        q = hq.to(dev, non_blocking=True).requires_grad_(True)
-        k = hk.to(dev, non_blocking=True).requires_grad_(True)
-        v = hv.to(dev, non_blocking=True).requires_grad_(True)
-        dy = hdy.to(dev, non_blocking=True)
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            if in_used[b]:
+                s_in.wait_event(in_free[b])
+            for t, h in zip(dev_in[b], host[b]):
+                t.copy_(h, non_blocking=True)
+            in_ready[b].record(s_in)
+        stream.wait_event(in_ready[b])
+        q, k, v = (t.detach().requires_grad_(True) for t in dev_in[b][:3])
+        dy = dev_in[b][3]
         y = ca.continuum_attention(q, k, v, lg_req, 64)
-        gq, gk, gv, gg = torch.autograd.grad(y, (q, k, v, lg_req), dy)
-        outs[0].copy_(gq, non_blocking=True)
-        outs[1].copy_(gk, non_blocking=True)
-        outs[2].copy_(gv, non_blocking=True)
-        gout.copy_(gg, non_blocking=True)
+        grads = torch.autograd.grad(y, (q, k, v, lg_req), dy)
+        in_free[b].record(stream)
+        in_used[b] = True
+        done = torch.cuda.Event()
+        done.record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            for hbuf, g in zip(outs[b], grads):
+                hbuf.copy_(g, non_blocking=True)
+            copied = torch.cuda.Event()
+            copied.record(s_out)
+        # a step's gradients are released only once the compute stream has waited
+        # for their copy-out, so the allocator never hands them out while in flight
+        held.append((grads, copied))
+        if len(held) > 2:
+            _, old_copied = held.pop(0)
+            stream.wait_event(old_copied)
 
     e2e_steps = max(3, min(args.steps, 20))
     with ca.use_impl(impl):
@@ -336,8 +364,12 @@ def run_ours(args, world, rank, local):
         _barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        s_in.wait_event(e0)
         for i in range(e2e_steps):
             e2e_step(i)
+        tail = torch.cuda.Event()
+        tail.record(s_out)
+        stream.wait_event(tail)
         e1.record(stream)
         torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(world, e0.elapsed_time(e1))
