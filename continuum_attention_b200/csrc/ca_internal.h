@@ -51,13 +51,13 @@ struct BwdWorkspace {
 
 namespace simt {
 constexpr int kForwardLaunches = 1;
-inline int backward_launches(const BwdArgs& a) { return a.dlog_gain ? 4 : 3; }
+inline int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ cast (+ d log_gain)
 cudaError_t forward(const FwdArgs& a);
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
 // backward helpers shared with the tcgen05 path
 cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc);  // D_i = dO_i . O_i, dq_acc = 0
-cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc);        // fp32 dQ -> dtype
-cudaError_t launch_gain_reduce(const BwdArgs& a, const float* part, int nparts);
+// fp32 dQ -> dtype, and (when a.dlog_gain) d log_gain from the per-key-tile partials, one launch
+cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* gain_part, int nparts);
 }  // namespace simt
 
 namespace sm100 {

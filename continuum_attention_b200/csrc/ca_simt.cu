@@ -532,30 +532,10 @@ __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ do
   if (row < rows && part == 0) rowdot[row] = s;
 }
 
-// fp32 -> dtype, 4 elements per thread (n a multiple of 4, 16-byte aligned source)
-template <typename T>
-__global__ void cast4_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n4) {
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n4; idx += (size_t)gridDim.x * blockDim.x) {
-    const float4 x = reinterpret_cast<const float4*>(src)[idx];
-    T out[4] = {from_f32<T>(x.x), from_f32<T>(x.y), from_f32<T>(x.z), from_f32<T>(x.w)};
-    if (sizeof(T) == 2)
-      reinterpret_cast<uint2*>(dst)[idx] = *reinterpret_cast<const uint2*>(out);
-    else
-      reinterpret_cast<float4*>(dst)[idx] = *reinterpret_cast<const float4*>(out);
-  }
-}
-
-template <typename T>
-__global__ void cast_rows_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n) {
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (size_t)gridDim.x * blockDim.x)
-    dst[idx] = from_f32<T>(src[idx]);
-}
-
-// d log_gain[h] = sum over batch and key-tile partials, fixed order (deterministic)
-__global__ void gain_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, int B,
-                                   int H, int nparts) {
-  const int h = blockIdx.x;
+// d log_gain[h] = sum over batch and key-tile partials, fixed order (deterministic);
+// one 256-thread block per head.
+__device__ __forceinline__ void gain_reduce_block(const float* __restrict__ part, float* __restrict__ out, int B,
+                                                  int H, int nparts, int h) {
   float s = 0.f;
   for (int idx = threadIdx.x; idx < B * nparts; idx += blockDim.x) {
     const int b = idx / nparts, t = idx % nparts;
@@ -569,6 +549,35 @@ __global__ void gain_reduce_kernel(const float* __restrict__ part, float* __rest
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += red[w];
     out[h] = t;
+  }
+}
+
+// The backward's last launch: fp32 dQ accumulator -> dtype in blocks
+// [0, cast_blocks) and, when part != nullptr, the d log_gain reduction of head
+// h in block cast_blocks + h.  kVec: 4 elements per thread (n a multiple of 4,
+// 16-byte aligned source, dst aligned to 4 elements); otherwise one per thread.
+template <typename T, bool kVec>
+__global__ void cast_gain_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n, int cast_blocks,
+                                 const float* __restrict__ part, float* __restrict__ gout, int B, int H,
+                                 int nparts) {
+  if ((int)blockIdx.x >= cast_blocks) {
+    gain_reduce_block(part, gout, B, H, nparts, (int)blockIdx.x - cast_blocks);
+    return;
+  }
+  const size_t stride = (size_t)cast_blocks * blockDim.x;
+  if (kVec) {
+    const size_t n4 = n / 4;
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n4; idx += stride) {
+      const float4 x = reinterpret_cast<const float4*>(src)[idx];
+      T out[4] = {from_f32<T>(x.x), from_f32<T>(x.y), from_f32<T>(x.z), from_f32<T>(x.w)};
+      if (sizeof(T) == 2)
+        reinterpret_cast<uint2*>(dst)[idx] = *reinterpret_cast<const uint2*>(out);
+      else
+        reinterpret_cast<float4*>(dst)[idx] = *reinterpret_cast<const float4*>(out);
+    }
+  } else {
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += stride)
+      dst[idx] = from_f32<T>(src[idx]);
   }
 }
 
@@ -659,29 +668,27 @@ cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc) {
 }
 
 template <typename T>
-static cudaError_t cast_dtype(const BwdArgs& a, const float* dq_acc) {
+static cudaError_t cast_dtype(const BwdArgs& a, const float* dq_acc, const float* part, int nparts) {
   const size_t n = (size_t)a.B * a.H * a.T * a.D;
-  if (n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.dq) & (4 * sizeof(T) - 1)) == 0) {
-    cast4_kernel<T><<<(unsigned)std::min<size_t>((n / 4 + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
-        dq_acc, (T*)a.dq, n / 4);
-  } else {
-    cast_rows_kernel<T><<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, a.stream>>>(
-        dq_acc, (T*)a.dq, n);
-  }
+  const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(a.dq) & (4 * sizeof(T) - 1)) == 0;
+  const size_t items = vec ? n / 4 : n;
+  const int cast_blocks = (int)std::min<size_t>(std::max<size_t>((items + 255) / 256, 1), 148 * 16);
+  const unsigned blocks = (unsigned)(cast_blocks + (a.dlog_gain ? a.H : 0));
+  if (vec)
+    cast_gain_kernel<T, true><<<blocks, 256, 0, a.stream>>>(dq_acc, (T*)a.dq, n, cast_blocks, part, a.dlog_gain,
+                                                           (int)a.B, (int)a.H, nparts);
+  else
+    cast_gain_kernel<T, false><<<blocks, 256, 0, a.stream>>>(dq_acc, (T*)a.dq, n, cast_blocks, part, a.dlog_gain,
+                                                            (int)a.B, (int)a.H, nparts);
   return cudaGetLastError();
 }
 
-cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc) {
+cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* gain_part, int nparts) {
   switch (a.dtype) {
-    case 0: return cast_dtype<float>(a, dq_acc);
-    case 1: return cast_dtype<__nv_bfloat16>(a, dq_acc);
-    default: return cast_dtype<__half>(a, dq_acc);
+    case 0: return cast_dtype<float>(a, dq_acc, gain_part, nparts);
+    case 1: return cast_dtype<__nv_bfloat16>(a, dq_acc, gain_part, nparts);
+    default: return cast_dtype<__half>(a, dq_acc, gain_part, nparts);
   }
-}
-
-cudaError_t launch_gain_reduce(const BwdArgs& a, const float* part, int nparts) {
-  gain_reduce_kernel<<<(unsigned)a.H, 256, 0, a.stream>>>(part, a.dlog_gain, (int)a.B, (int)a.H, nparts);
-  return cudaGetLastError();
 }
 
 template <typename T>
@@ -692,10 +699,7 @@ static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
   else if (a.D <= 64) e = launch_bwd<T, 64>(a, w);
   else e = launch_bwd<T, 128>(a, w);
   if (e != cudaSuccess) return e;
-  e = launch_cast_dq(a, w.dq_acc);
-  if (e != cudaSuccess) return e;
-  if (a.dlog_gain) e = launch_gain_reduce(a, w.gain_part, (int)((a.T + BK - 1) / BK));
-  return e;
+  return launch_cast_dq(a, w.dq_acc, w.gain_part, (int)((a.T + BK - 1) / BK));
 }
 
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w) {

@@ -1165,7 +1165,7 @@ bool backward_supported(const BwdArgs& a) {
          aligned16(a.d_o) && aligned16(a.dk) && aligned16(a.dv) && encode_fn() != nullptr;
 }
 int forward_launches(const FwdArgs&) { return 1; }
-int backward_launches(const BwdArgs& a) { return a.dlog_gain ? 4 : 3; }
+int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ cast (+ d log_gain)
 
 template <bool kBF16>
 static cudaError_t launch_fwd(const FwdArgs& a) {
@@ -1204,10 +1204,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
       a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  e = simt::launch_cast_dq(a, w.dq_acc);
-  if (e != cudaSuccess) return e;
-  if (a.dlog_gain) e = simt::launch_gain_reduce(a, w.gain_part, (int)nkt);
-  return e;
+  return simt::launch_cast_dq(a, w.dq_acc, w.gain_part, (int)nkt);
 }
 
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w) {
