@@ -32,6 +32,8 @@ SIGNATURES = {
                                    _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_device_status": (_int, [_int]),
     "ca_last_launch_count": (_int, []),
+    "ca_rope_qkv_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
+    "ca_rope_qkv_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
 }
 
 _lock = threading.Lock()

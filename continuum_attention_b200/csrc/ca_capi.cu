@@ -170,6 +170,46 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
   return ok();
 }
 
+static int check_rope(const char* fn, const void* a, const void* b, const void* c, const void* d,
+                      const float* cs, int64_t B, int64_t T, int64_t H, int64_t D, int dtype) {
+  if (B < 0 || T < 0 || H < 0 || D < 0)
+    return fail(CA_ERR_INVALID_ARGUMENT, "%s: negative shape [B,T,H,D]=[%lld,%lld,%lld,%lld]", fn, (long long)B,
+                (long long)T, (long long)H, (long long)D);
+  if (dtype < CA_DTYPE_F32 || dtype > CA_DTYPE_F16)
+    return fail(CA_ERR_INVALID_ARGUMENT, "%s: unknown dtype code %d", fn, dtype);
+  if (D % 8 != 0 || D > 256)
+    return fail(CA_ERR_UNSUPPORTED, "%s: head dim D=%lld must be a multiple of 8 and <= 256", fn, (long long)D);
+  if (B * T * H * D == 0) return CA_OK;
+  if (!a || !b || !c || !d || !cs) return fail(CA_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+  const uintptr_t m = (uintptr_t)a | (uintptr_t)b | (uintptr_t)c | (uintptr_t)d | (uintptr_t)cs;
+  if (m & 15) return fail(CA_ERR_INVALID_ARGUMENT, "%s: buffers must be 16-byte aligned", fn);
+  return CA_OK;
+}
+
+int ca_rope_qkv_forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, int64_t B, int64_t T,
+                        int64_t H, int64_t D, int dtype, void* stream) {
+  int st = check_rope("ca_rope_qkv_forward", qkv, q, k, v, cos_sin, B, T, H, D, dtype);
+  if (st != CA_OK) return st;
+  g_last_launches = 0;
+  if (B * T * H * D == 0) return ok();
+  cudaError_t e = ca::rope::forward(qkv, cos_sin, q, k, v, B, T, H, D, dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_rope_qkv_forward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
+int ca_rope_qkv_backward(const void* dq, const void* dk, const void* dv, const float* cos_sin, void* dqkv,
+                         int64_t B, int64_t T, int64_t H, int64_t D, int dtype, void* stream) {
+  int st = check_rope("ca_rope_qkv_backward", dq, dk, dv, dqkv, cos_sin, B, T, H, D, dtype);
+  if (st != CA_OK) return st;
+  g_last_launches = 0;
+  if (B * T * H * D == 0) return ok();
+  cudaError_t e = ca::rope::backward(dq, dk, dv, cos_sin, dqkv, B, T, H, D, dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_rope_qkv_backward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
 int ca_device_status(int reset) {
   int value = 0;
   cudaError_t e = ca::read_device_status(&value, reset != 0);

@@ -71,6 +71,15 @@ cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
 }  // namespace sm100
 
 // device status word (bounded waits record CA_ERR_DEVICE_TIMEOUT here)
+namespace rope {
+// qkv [B][T][3][H][D] -> q, k (rotary embedding applied), v [B][H][T][D]; cos_sin float32 [T][D/2][2]
+cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, long long B, long long T,
+                    long long H, long long D, int dtype, cudaStream_t s);
+// dq, dk, dv [B][H][T][D] -> dqkv [B][T][3][H][D] (transposed rotation on dq, dk)
+cudaError_t backward(const void* dq, const void* dk, const void* dv, const float* cos_sin, void* dqkv,
+                     long long B, long long T, long long H, long long D, int dtype, cudaStream_t s);
+}  // namespace rope
+
 cudaError_t read_device_status(int* out, bool reset);
 
 }  // namespace ca

@@ -9,7 +9,9 @@ untied embedding and head, RMSNorm, RoPE theta 1e4, residual projections
 initialised with std 0.02/sqrt(2 n_layers)).
 
 ``attention_fn`` defaults to the CUDA operator; tests on machines without a GPU
-pass a CPU stand-in with the same signature.
+pass a CPU stand-in with the same signature.  On CUDA the attention block's
+input side is one native kernel (``rope.rope_qkv``: QKV unpacking fused with the
+rotary embedding) and the norms are fused ``F.rms_norm`` kernels.
 """
 from __future__ import annotations
 
@@ -22,6 +24,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import continuum_attention
+from .rope import apply_rope_torch, rope_qkv
 
 
 @dataclass
@@ -51,32 +54,20 @@ class ContinuumDecoderConfig:
 
 
 class RMSNorm(nn.Module):
+    """weight * x * rsqrt(mean(x^2) + eps) (cuda/continuum_attention.py:815-821), one fused kernel."""
+
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(dim))
         self.eps = eps
 
     def forward(self, x):
-        return self.weight * x * torch.rsqrt(x.square().mean(-1, keepdim=True) + self.eps)
-
-
-def rope_tables(T: int, D: int, theta: float, device, dtype):
-    """cos/sin tables [1,1,T,D] with each frequency repeated for its (even, odd) pair."""
-    freq = 1.0 / (theta ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
-    phase = torch.outer(torch.arange(T, device=device, dtype=torch.float32), freq)
-    cos = torch.repeat_interleave(phase.cos(), 2, -1).to(dtype)[None, None]
-    sin = torch.repeat_interleave(phase.sin(), 2, -1).to(dtype)[None, None]
-    return cos, sin
+        return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 
 def apply_rope(q, k, theta: float):
     """Rotary embedding on interleaved (even, odd) pairs (cuda/continuum_attention.py:825-835)."""
-    cos, sin = rope_tables(q.shape[-2], q.shape[-1], theta, q.device, q.dtype)
-
-    def rotate(t):
-        return torch.stack((-t[..., 1::2], t[..., 0::2]), -1).flatten(-2)
-
-    return q * cos + rotate(q) * sin, k * cos + rotate(k) * sin
+    return apply_rope_torch(q, k, theta)
 
 
 class ContinuumSelfAttention(nn.Module):
@@ -96,9 +87,7 @@ class ContinuumSelfAttention(nn.Module):
 
     def forward(self, x):
         B, T, C = x.shape
-        qkv = self.qkv(x).reshape(B, T, 3, self.heads, self.head_dim).permute(2, 0, 3, 1, 4)
-        q, k, v = qkv.unbind(0)
-        q, k = apply_rope(q, k, self.rope_theta)
+        q, k, v = rope_qkv(self.qkv(x), self.heads, self.rope_theta)
         y = self.attention_fn(q, k, v, self.log_qk_gain, self.ca_query_tile)
         return self.out(y.transpose(1, 2).contiguous().reshape(B, T, C))
 

@@ -99,8 +99,11 @@ def gather_bh(part: torch.Tensor, B: int, H: int, group=None) -> torch.Tensor:
 
 
 def build_adamw(model, lr: float = 3e-4, weight_decay: float = 0.1, betas=(0.9, 0.95)):
-    """AdamW as the reference builds it (cuda/runtime.py:87-88)."""
-    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=weight_decay, betas=betas)
+    """AdamW as the reference builds it (cuda/runtime.py:87-88); on CUDA parameters the
+    fused implementation (one kernel per step for all parameters)."""
+    params = list(model.parameters())
+    fused = bool(params) and all(p.is_cuda for p in params)
+    return torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, betas=betas, fused=fused)
 
 
 def train_step(model, optimizer, batch: torch.Tensor, amp_dtype=torch.bfloat16, grad_clip: float = 1.0):

@@ -135,8 +135,30 @@ int ca_backward_noalloc(const void* q, const void* k, const void* v, const void*
                         int64_t B, int64_t H, int64_t T, int64_t D,
                         int dtype, int impl, void* stream);
 
-/* Number of kernels the last successful ca_forward / ca_backward call on this
- * thread enqueued (memsets excluded).  Diagnostic for launch accounting. */
+/*
+ * CA-S decoder attention block, input side: rotary position embedding fused
+ * with the unpacking of the QKV projection.  Replaces apply_rope
+ * (cuda/continuum_attention.py:825-835) together with the reshape / permute /
+ * unbind of ContinuumSelfAttention.forward (:850-852) and the contiguity
+ * copies continuum_attention makes of its operands (:783).
+ *   qkv      [B][T][3][H][D]  the projection output (q, k, v along axis 2)
+ *   cos_sin  float32 [T][D/2][2]: (cos, sin)(t * theta^(-2p/D)) for pair p
+ *   q, k, v  [B][H][T][D] outputs; q and k rotated pairwise
+ *            (x_{2p}, x_{2p+1}) -> (x_{2p} c - x_{2p+1} s, x_{2p+1} c + x_{2p} s)
+ * dtype as for the operator; D a multiple of 8, at most 256; every buffer
+ * 16-byte aligned.  One launch, no allocation.
+ */
+int ca_rope_qkv_forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v,
+                        int64_t B, int64_t T, int64_t H, int64_t D, int dtype, void* stream);
+
+/* Gradient of ca_rope_qkv_forward: dq, dk, dv [B][H][T][D] -> dqkv
+ * [B][T][3][H][D] with the transposed rotation on dq and dk. */
+int ca_rope_qkv_backward(const void* dq, const void* dk, const void* dv, const float* cos_sin, void* dqkv,
+                         int64_t B, int64_t T, int64_t H, int64_t D, int dtype, void* stream);
+
+/* Number of kernels the last successful ca_forward / ca_backward /
+ * ca_rope_qkv_* call on this thread enqueued (memsets excluded).  Diagnostic
+ * for launch accounting. */
 int ca_last_launch_count(void);
 
 /*
