@@ -53,20 +53,24 @@ def _validate(q, k, v, log_gain):
         raise ValueError(f"log_gain must have shape [H]=[{H}], got {tuple(log_gain.shape)}")
 
 
-def forward_raw(q, k, v, log_gain_f32, impl="auto", want_f32=False):
-    """Run the native forward; returns (o, row_stats, o_f32 or None).
+def forward_raw(q, k, v, log_gain_f32, impl="auto", want_f32=False, want_stats=True):
+    """Run the native forward; returns (o, row_stats or None, o_f32 or None).
 
     q, k, v contiguous CUDA [B,H,T,D]; log_gain_f32 contiguous float32 [H] on the
-    same device.  Used by the autograd op, the tests and the benchmark.
+    same device.  ``want_stats=False`` is the inference form (no backward follows,
+    the per-row statistics are not written).  Used by the autograd op, the tests
+    and the benchmark.
     """
     B, H, T, D = q.shape
     lib = _native.lib()
     o = torch.empty_like(q)
-    stats = torch.empty(B * H * T * lib.ca_row_stats_floats(), dtype=torch.float32, device=q.device)
+    stats = (torch.empty(B * H * T * lib.ca_row_stats_floats(), dtype=torch.float32, device=q.device)
+             if want_stats else None)
     o32 = torch.empty(q.shape, dtype=torch.float32, device=q.device) if want_f32 else None
     with torch.cuda.device(q.device):
         st = lib.ca_forward(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), ctypes_ptr(log_gain_f32),
-                            ctypes_ptr(o), None if o32 is None else ctypes_ptr(o32), ctypes_ptr(stats),
+                            ctypes_ptr(o), None if o32 is None else ctypes_ptr(o32),
+                            None if stats is None else ctypes_ptr(stats),
                             B, H, T, D, _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _stream(q.device))
     _native.check("ca_forward", st)
     return o, stats, o32
@@ -115,6 +119,10 @@ class ContinuumAttentionFunction(torch.autograd.Function):
         _validate(q, k, v, log_gain)
         lg = log_gain.detach().to(device=q.device, dtype=torch.float32).contiguous()
         lowp = q.dtype != torch.float32
+        if not any(ctx.needs_input_grad[:4]):
+            # inference: no backward can follow, so no statistics or fp32 output are kept
+            o, _, _ = forward_raw(q, k, v, lg, impl=_current_impl(), want_stats=False)
+            return o
         o, stats, o32 = forward_raw(q, k, v, lg, impl=_current_impl(), want_f32=lowp)
         ctx.save_for_backward(q, k, v, o32 if lowp else o, stats, lg)
         ctx.lowp = lowp

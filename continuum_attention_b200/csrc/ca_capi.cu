@@ -94,8 +94,8 @@ int ca_forward(const void* q, const void* k, const void* v, const float* log_gai
   int st = check_shape(B, H, T, D, dtype, impl);
   if (st != CA_OK) return st;
   if (B * H * T == 0) return ok();
-  if (!q || !k || !v || !log_gain || !o || !row_stats)
-    return fail(CA_ERR_INVALID_ARGUMENT, "ca_forward: null q/k/v/log_gain/o/row_stats pointer");
+  if (!q || !k || !v || !log_gain || !o)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_forward: null q/k/v/log_gain/o pointer");
   ca::FwdArgs a{q, k, v, log_gain, o, o_f32, row_stats, B, H, T, D, dtype,
                 (float)(1.0 / std::sqrt((double)D)), (cudaStream_t)stream};
   cudaError_t e;

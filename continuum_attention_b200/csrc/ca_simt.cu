@@ -217,7 +217,7 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       if (o32) o32[base + (size_t)i * D + d] = y;
     }
   }
-  if (quad == 0) {
+  if (quad == 0 && stats) {   // stats == nullptr: inference, no backward follows
     stats[2 * ((size_t)bh * Tn + i)] = m_run;
     stats[2 * ((size_t)bh * Tn + i) + 1] = Z;
   }

@@ -454,8 +454,10 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     for (int c = 0; c < HD / 4; ++c)
       d32[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
   }
-  stats[2 * row] = m_used;
-  stats[2 * row + 1] = z;
+  if (stats) {   // nullptr: inference, no backward follows
+    stats[2 * row] = m_used;
+    stats[2 * row + 1] = z;
+  }
 }
 
 template <bool kBF16>

@@ -81,7 +81,8 @@ int ca_row_stats_floats(void);
 
 /*
  * Forward.  o = CA(q, k, v) [B,H,T,D] in dtype; row_stats receives the
- * per-row statistics the backward needs (row max and normaliser).
+ * per-row statistics the backward needs (row max and normaliser).  For
+ * inference row_stats may be NULL: nothing but o (and o_f32) is written.
  * o_f32 (optional, may be NULL) additionally receives the float32
  * accumulator before the final rounding to dtype (o is exactly the
  * round-to-nearest-even of o_f32 when both are written).

@@ -153,3 +153,18 @@ def test_fixed_tau_matches_learned_gain_at_same_value():
     a = ca.continuum_attention_fixed_tau(q, k, v, 0.30)
     b = ca.continuum_attention(q, k, v, torch.full((4,), math.log(1 / 0.30), device=DEV))
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_inference_forward_without_statistics(dtype):
+    # no input requires grad: the op runs the inference form (row statistics not
+    # written) and returns exactly the training forward's output
+    q, k, v, dy = gen_inputs((2, 3, 300, 64), seed=11)
+    q, k, v = (t.to(DEV, dtype) for t in (q, k, v))
+    lg = torch.tensor([0.0, 0.3, -0.2], device=DEV)
+    with torch.no_grad():
+        y_inf = ca.continuum_attention(q, k, v, lg)
+    y_train = ca.continuum_attention(q.clone().requires_grad_(True), k, v, lg)
+    assert torch.equal(y_inf, y_train.detach())
+    o, stats, o32 = ca.forward_raw(q, k, v, lg, want_stats=False)
+    assert stats is None and o32 is None and torch.equal(o, y_inf)
