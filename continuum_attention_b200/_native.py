@@ -34,6 +34,7 @@ SIGNATURES = {
     "ca_last_launch_count": (_int, []),
     "ca_rope_qkv_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
     "ca_rope_qkv_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
+    "ca_selftest_wait_timeout": (_int, [_i64, _vp]),
 }
 
 _lock = threading.Lock()

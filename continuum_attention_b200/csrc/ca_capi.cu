@@ -210,6 +210,18 @@ int ca_rope_qkv_backward(const void* dq, const void* dk, const void* dv, const f
   return ok();
 }
 
+int ca_selftest_wait_timeout(int64_t limit_us, void* stream) {
+  if (limit_us < 1 || limit_us > 10000000)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_selftest_wait_timeout: limit_us=%lld outside [1, 1e7]",
+                (long long)limit_us);
+  g_last_launches = 0;
+  cudaError_t e = ca::sm100::launch_wait_timeout_selftest((unsigned long long)limit_us * 1000ull,
+                                                          (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_selftest_wait_timeout launch");
+  g_last_launches = 1;
+  return ok();
+}
+
 int ca_device_status(int reset) {
   int value = 0;
   cudaError_t e = ca::read_device_status(&value, reset != 0);

@@ -68,6 +68,8 @@ int forward_launches(const FwdArgs& a);
 int backward_launches(const BwdArgs& a);
 cudaError_t forward(const FwdArgs& a);
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
+// one CTA whose bounded mbarrier wait runs out after limit_ns (nothing completes the barrier)
+cudaError_t launch_wait_timeout_selftest(unsigned long long limit_ns, cudaStream_t s);
 }  // namespace sm100
 
 // device status word (bounded waits record CA_ERR_DEVICE_TIMEOUT here)

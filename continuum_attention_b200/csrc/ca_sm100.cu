@@ -1213,6 +1213,27 @@ cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w) {
   return a.dtype == 1 ? launch_bwd<true>(a, w) : launch_bwd<false>(a, w);
 }
 
+// Self-test of the bounded waits: one CTA waits on an mbarrier that nothing
+// arrives on.  The wait gives up after limit_ns, records CA_ERR_DEVICE_TIMEOUT in
+// the status word and the kernel returns -- no fault, trap or hang -- so a test
+// can check that a timed-out device wait is reported and leaves the context usable.
+__global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) mbar_wait(&bar, 0, &abort_flag, limit_ns);
+}
+
+cudaError_t launch_wait_timeout_selftest(unsigned long long limit_ns, cudaStream_t s) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, s>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 }  // namespace sm100
 
 cudaError_t read_device_status(int* out, bool reset) {

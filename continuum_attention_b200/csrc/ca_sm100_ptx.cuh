@@ -70,16 +70,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for the phase with the given parity.  Gives up after kWaitLimitNs,
-// records CA_ERR_DEVICE_TIMEOUT in g_device_status and sets *abort_flag.
-// Any number of threads may wait on the same barrier.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Wait for the phase with the given parity.  Gives up after limit_ns
+// (kWaitLimitNs by default), records CA_ERR_DEVICE_TIMEOUT in g_device_status
+// and sets *abort_flag.  Any number of threads may wait on the same barrier.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicCAS(&g_device_status, 0, 5);
       *abort_flag = 1;
       return false;

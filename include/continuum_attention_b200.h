@@ -170,6 +170,17 @@ int ca_last_launch_count(void);
  */
 int ca_device_status(int reset);
 
+/*
+ * Diagnostics (no reference counterpart): enqueue one CTA that waits, with the
+ * kernels' bounded-wait routine, on an mbarrier nothing ever completes.  The
+ * wait gives up after limit_us microseconds (1 .. 1e7), records
+ * CA_ERR_DEVICE_TIMEOUT in the device status word and the kernel returns, so a
+ * caller can check that device-side timeouts are reported by
+ * ca_device_status() and that the context stays usable.  No fault, trap or
+ * hang is involved.
+ */
+int ca_selftest_wait_timeout(int64_t limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -168,3 +168,22 @@ def test_inference_forward_without_statistics(dtype):
     assert torch.equal(y_inf, y_train.detach())
     o, stats, o32 = ca.forward_raw(q, k, v, lg, want_stats=False)
     assert stats is None and o32 is None and torch.equal(o, y_inf)
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives():
+    # a device wait on a barrier nothing completes gives up after its limit,
+    # the status word reports CA_ERR_DEVICE_TIMEOUT (5), and the next calls work
+    from continuum_attention_b200 import _native
+    lib = _native.lib()
+    lib.ca_device_status(1)
+    assert lib.ca_selftest_wait_timeout(50000, None) == 0          # 50 ms limit
+    assert lib.ca_device_status(1) == 5
+    assert lib.ca_device_status(0) == 0
+    assert lib.ca_selftest_wait_timeout(0, None) == 1
+    q, k, v, dy = gen_inputs((1, 2, 200, 64), seed=5)
+    q, k, v = (t.to(DEV, torch.bfloat16) for t in (q, k, v))
+    lg = torch.zeros(2, device=DEV)
+    y1 = ca.continuum_attention(q, k, v, lg)
+    y2 = ca.continuum_attention(q, k, v, lg)
+    assert torch.isfinite(y1.float()).all() and torch.equal(y1, y2)
+    assert lib.ca_device_status(0) == 0
