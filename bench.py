@@ -20,7 +20,9 @@ a copy-in, a compute and a copy-out stream.
 The line also carries "decoder": the CA-S decoder training step (BASELINE
 config 4, 101,205,120 parameters, 8 x 2048 random bytes per GPU, bf16 autocast,
 AdamW) in tokens/s over all ranks, with DDP over NCCL when N > 1
-(``--no-decoder`` skips it).
+(``--no-decoder`` skips it), and at N=1 "tinylm": the reference's 5M-parameter
+TinyLM in its fixed-tau CA variant P (fp32, batch 8, T = 192 and 512), the
+training step run as one CUDA graph (``--no-tinylm`` skips it).
 
 ``--impl reference`` times the reference algorithm's CPU path (the float32
 restatement in oracle/, all host threads) on a bounded sample of the same
@@ -260,6 +262,52 @@ def run_decoder(args, world, rank, local, steps: int, warmup: int):
             "final_loss": float(loss.item()) if loss is not None else None, "data": "synthetic uniform bytes"}
 
 
+def run_tinylm(local, steps: int = 50):
+    """TinyLM P (fixed tau 0.30, fp32 as the reference trains it) training tokens/s on
+    one GPU at the reference's defaults (batch 8, T = 192) and at T = 512: the
+    whole step as a CUDA graph, and eagerly for comparison."""
+    from continuum_attention_b200.tinylm import TinyLM, TinyLMTrainer, build_optimizer, train_step
+    dev = torch.device("cuda", local)
+    out = {"metric": "TinyLM-P train tokens/s (architecture.py TinyLM, 5,008,640 params, fp32)",
+           "unit": "tokens/s", "batch": 8, "data": "synthetic uniform bytes"}
+    g = torch.Generator(device="cpu").manual_seed(1729)
+    for T in (192, 512):
+        torch.manual_seed(1729)
+        model = TinyLM(variant="P", seq_len=T).to(dev)
+        batch = torch.randint(0, 256, (8, T + 1), generator=g).to(dev)
+        x, y = batch[:, :-1].contiguous(), batch[:, 1:].contiguous()
+        trainer = TinyLMTrainer(model, batch_size=8, seq_len=T)
+        for _ in range(5):
+            trainer.step(x, y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            trainer.step(x, y)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        out[f"T{T}_graph_tokens_per_s"] = 8 * T / (ms * 1e-3)
+        out[f"T{T}_graph_ms_per_step"] = ms
+        if T == 192:
+            torch.manual_seed(1729)
+            eager = TinyLM(variant="P", seq_len=T).to(dev)
+            opt = build_optimizer(eager)
+            for _ in range(5):
+                train_step(eager, opt, x, y)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(steps):
+                train_step(eager, opt, x, y)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            out["T192_eager_tokens_per_s"] = 8 * T / (ms * 1e-3)
+        del trainer, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, world, rank, local):
     import continuum_attention_b200 as ca
     from continuum_attention_b200 import _native
@@ -403,6 +451,7 @@ def run_ours(args, world, rank, local):
     decoder = None
     if not args.no_decoder:
         decoder = run_decoder(args, world, rank, local, steps=args.decoder_steps, warmup=3)
+    tinylm = run_tinylm(local) if (world == 1 and not args.no_tinylm) else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -422,6 +471,7 @@ def run_ours(args, world, rank, local):
             "clocks": clocks,
             "gpu_launches": launches,
             "decoder": decoder,
+            "tinylm": tinylm,
         }
         print(json.dumps(line), flush=True)
 
@@ -436,6 +486,7 @@ def main():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-decoder", action="store_true", help="skip the CA-S decoder tokens/s measurement")
     p.add_argument("--decoder-steps", type=int, default=10)
+    p.add_argument("--no-tinylm", action="store_true", help="skip the TinyLM-P small-model measurement")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
