@@ -1,25 +1,28 @@
 // ca_sm100.cu -- sm_100a tensor-core Continuum Attention kernels (bf16 / f16,
 // head dim 64): TMA-staged Q/K/V tiles, tcgen05.mma with TMEM accumulators.
 //
-// Forward, one CTA per 128-row query tile (two CTAs per SM):
+// Forward, one CTA per 128-row query tile (two CTAs per SM), keys in half-tiles
+// of 64 that rotate through three 64-column S/P regions of TMEM:
 //   warp 4 is the producer (the whole warp runs converged; lane 0 issues): TMA
-//     loads of Q (once) and of
-//     K/V tiles into a 2-stage ring, and the tcgen05.mma issue:
-//       S(j)  = Q K_j^T              128x128 fp32 in TMEM columns [0,128)
-//       O    += P_hi(j) V'_j + P_lo(j) V'_j   128x64 fp32 in TMEM columns [128,192),
-//               issued in two halves of 64 keys: the first as soon as the math
-//               warps have written P for keys 0..63, overlapping the second half
-//     where V'_j is the V tile staged one row early (keys j0-1 .. j0+126) and
-//     P(j) is written by the math warps over the same TMEM columns as S(j).
+//     loads of Q (once) and of K / V' half-tiles into a 4-stage ring, and the
+//     tcgen05.mma issue:
+//       S_h  = Q K_h^T              128x64 fp32 in region h % 3
+//       O   += P_hi,h V'_h + P_lo,h V'_h   128x64 fp32 in TMEM columns [192,256)
+//     where V'_h is the V half-tile staged one row early (keys 64h-1 .. 64h+62)
+//     and P_h is written by the math warps over the same columns as S_h (each
+//     16-key chunk's 16 columns become 8 columns of bf16 hi pairs and 8 of lo
+//     pairs).  S_{h+3} is issued right after P V'_h, into the region P_h leaves,
+//     so S of the next two half-tiles is ready while the math warps work.
 //   warps 0-3 (thread = query row = TMEM lane) load their S row, keep an online
-//     row max (rescaling O only when the max grows by more than 8 nats), form
-//     the segment moments, and store P split into bf16 hi + lo parts, so the
-//     P V product keeps ~16 significant bits of every weight.
-// P column c of key tile j0 holds the weight of key j0-1+c:
-//   P[c] = B_{j0+c-1} + A_{j0+c} (+ half caps on key 0 and key i),
+//     row max per half-tile (rescaling O only when the max grows by more than 8
+//     nats, after the previous P V' has landed), form the segment moments, and
+//     store P split into bf16 hi + lo parts, so the P V product keeps ~16
+//     significant bits of every weight.
+// P column c of the half-tile starting at key kb holds the weight of key kb-1+c:
+//   P[c] = B_{kb+c-1} + A_{kb+c} (+ half caps on key 0 and key i),
 // with A_k = M0-M1 and B_k = M1 of segment k (key k-1 -> key k); B of the last
-// key of a tile is carried to the next tile, and a weight still pending after
-// the diagonal tile (query i on the last column) is added in the epilogue.
+// key of a half-tile is carried to the next one, and a weight still pending
+// after the last half-tile (query i on its last key) is added in the epilogue.
 // Replaces the reference's per-query-tile chain bmm(QK^T) -> scale ->
 // ca_forward_half_kernel -> bmm(W V) (cuda/continuum_attention.py:670-690).
 //
@@ -38,28 +41,29 @@ namespace sm100 {
 namespace fwd {
 
 constexpr int BM = 128;            // query rows per CTA (= TMEM lanes)
-constexpr int BN = 128;            // keys per tile
+constexpr int HB = 64;             // keys per half-tile, the pipeline unit
 constexpr int HD = 64;             // head dim
-constexpr int STAGES = 2;
+constexpr int NREG = 3;            // rotating S/P regions of 64 TMEM columns
+constexpr int KSTAGES = 4;         // K / V' half-tile ring
 constexpr int NUM_THREADS = 160;   // 4 math warps + 1 producer warp
-constexpr uint32_t TILE_BYTES = BN * HD * 2;
+constexpr uint32_t Q_BYTES = BM * HD * 2;      // 16 KB
+constexpr uint32_t HALF_BYTES = HB * HD * 2;   // 8 KB
 constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t TMEM_S = 0;     // S(j): columns [0,128); P_hi(j) overwrites [0,64)
-constexpr uint32_t TMEM_O = 128;   // O accumulator: columns [128,192)
-constexpr uint32_t TMEM_PLO = 192; // P_lo(j): columns [192,256)
+constexpr uint32_t TMEM_O = 192;   // O accumulator: columns [192,256); region r: [64r, 64r+64)
 constexpr float kRescaleNats = 8.0f;
 
 struct __align__(1024) Smem {
-  uint8_t q[TILE_BYTES];
-  uint8_t k[STAGES][TILE_BYTES];
-  uint8_t v[STAGES][TILE_BYTES];
+  uint8_t q[Q_BYTES];
+  uint8_t k[KSTAGES][HALF_BYTES];
+  uint8_t v[KSTAGES][HALF_BYTES];
   uint64_t bar_q;
-  uint64_t bar_k[STAGES];
-  uint64_t bar_v[STAGES];
-  uint64_t bar_kv_free[STAGES];
-  uint64_t bar_s_full;
-  uint64_t bar_p_half;               // P of keys 0..63 of the tile is in TMEM
-  uint64_t bar_p_ready;              // all of P is in TMEM
+  uint64_t bar_k[KSTAGES];
+  uint64_t bar_v[KSTAGES];
+  uint64_t bar_kv_free[KSTAGES];   // the half-tile's P V' has completed (its S long before)
+  uint64_t bar_s_full[NREG];       // S of a half-tile is in region r
+  uint64_t bar_p_ready[NREG];      // P of the half-tile in region r is in TMEM
+  uint64_t bar_pv_done[2];         // half-tile h's P V' (and every MMA before it) has
+                                   // completed: barrier h & 1, phase h >> 1
   uint64_t bar_o_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -67,6 +71,7 @@ struct __align__(1024) Smem {
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack
 
+// S = Q K_h^T for one half-tile: M = 128 queries, N = 64 keys, K = 64 (4 MMAs)
 __device__ __forceinline__ void issue_s(uint32_t q_saddr, uint32_t k_saddr, uint32_t d_tmem, uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < HD / 16; ++kk) {
@@ -76,84 +81,90 @@ __device__ __forceinline__ void issue_s(uint32_t q_saddr, uint32_t k_saddr, uint
   }
 }
 
-// O += P V' over keys 64h .. 64h+63 of the tile (h = 0, 1), hi and lo parts.
-__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, uint32_t idesc,
-                                              int h, bool accumulate) {
+// O += P V'_h over the half-tile's 64 keys: hi and lo parts of P, 16 keys per MMA,
+// A from TMEM (16 columns per 16 keys: 8 of hi pairs, then 8 of lo pairs)
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, uint32_t idesc,
+                                         bool accumulate) {
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
 #pragma unroll
-    for (int k4 = 0; k4 < BN / 32; ++k4) {
-      const int kk = 4 * h + k4;
-      const uint64_t b = sdesc_sw128(v_saddr + kk * 2048, 16384, 1024);   // V: MN-major
+    for (int kk = 0; kk < HB / 16; ++kk) {
+      const uint64_t b = sdesc_sw128(v_saddr + kk * 2048, 16384, 1024);   // V': MN-major
       const uint32_t acc = (accumulate || part > 0 || kk > 0) ? 1u : 0u;
-      mma_ts(o_tmem, p_tmem + (part ? TMEM_PLO : TMEM_S) + kk * 8, b, idesc, acc);
+      mma_ts(o_tmem, p_tmem + 16 * kk + 8 * part, b, idesc, acc);
     }
   }
 }
 
+// Producer schedule over half-tiles h = 0 .. nh-1 (region h % 3, ring stage h % 4):
+//   S_0, S_1, S_2 up front; then per h: wait P_h -> P V'_h (commit pv_done and
+//   kv_free) -> S_{h+3} into the region P_h just left (tcgen05 MMAs run in issue
+//   order, so it overwrites P_h only after P V'_h has read it) -> refill the ring
+//   stage of h with half-tile h+4 once P V'_h has completed.  The math warps thus
+//   find S of their next half-tile already computed.
 template <bool kBF16>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv, int bh,
-                         int q0, int n_tiles, uint32_t tmem) {
+                         int q0, int nh, uint32_t tmem) {
   volatile int* ab = &sm.abort_flag;
-  const uint32_t id_s = make_idesc(BM, BN, kBF16, false);
+  const uint32_t id_s = make_idesc(BM, HB, kBF16, false);
   const uint32_t id_o = make_idesc(BM, HD, kBF16, true);
-  bool k_pending[STAGES] = {false, false}, v_pending[STAGES] = {false, false};
-  uint32_t k_phase[STAGES] = {0, 0}, v_phase[STAGES] = {0, 0};
+  bool k_pending[KSTAGES], v_pending[KSTAGES];
+  uint32_t k_phase[KSTAGES], v_phase[KSTAGES];
+  for (int s2 = 0; s2 < KSTAGES; ++s2) {
+    k_pending[s2] = v_pending[s2] = false;
+    k_phase[s2] = v_phase[s2] = 0;
+  }
   bool q_pending = true;
-  bool mma_issued = false;
 
-  mbar_arrive_expect_tx(&sm.bar_q, TILE_BYTES);
+  mbar_arrive_expect_tx(&sm.bar_q, Q_BYTES);
   tma_load_3d(sm.q, tq, &sm.bar_q, 0, q0, bh);
-  for (int t = 0; t < STAGES && t < n_tiles; ++t) {
-    mbar_arrive_expect_tx(&sm.bar_k[t], TILE_BYTES);
-    tma_load_3d(sm.k[t], tk, &sm.bar_k[t], 0, t * BN, bh);
-    mbar_arrive_expect_tx(&sm.bar_v[t], TILE_BYTES);
-    tma_load_3d(sm.v[t], tv, &sm.bar_v[t], 0, t * BN - 1, bh);
+  for (int t = 0; t < KSTAGES && t < nh; ++t) {
+    mbar_arrive_expect_tx(&sm.bar_k[t], HALF_BYTES);
+    tma_load_3d(sm.k[t], tk, &sm.bar_k[t], 0, t * HB, bh);
+    mbar_arrive_expect_tx(&sm.bar_v[t], HALF_BYTES);
+    tma_load_3d(sm.v[t], tv, &sm.bar_v[t], 0, t * HB - 1, bh);
     k_pending[t] = v_pending[t] = true;
   }
-  const uint32_t q_sa = smem_u32(sm.q);
-  const uint32_t s_tmem = tmem + TMEM_S, o_tmem = tmem + TMEM_O;
-
-  if (mbar_wait_warp(&sm.bar_q, 0, ab) && mbar_wait_warp(&sm.bar_k[0], 0, ab)) {
-    q_pending = false;
-    k_pending[0] = false;
-    k_phase[0] ^= 1;
+  const uint32_t q_sa = smem_u32(sm.q), o_tmem = tmem + TMEM_O;
+  bool good = mbar_wait_warp(&sm.bar_q, 0, ab);
+  if (good) q_pending = false;
+  for (int h = 0; good && h < NREG && h < nh; ++h) {
+    good = mbar_wait_warp(&sm.bar_k[h], 0, ab);
+    if (!good) break;
+    k_pending[h] = false;
+    k_phase[h] ^= 1;
     tc_fence_after();
-    issue_s(q_sa, smem_u32(sm.k[0]), s_tmem, id_s);
-    mma_commit(&sm.bar_s_full);
-    mma_issued = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j % STAGES;
-      // the first half of P V' runs while the math warps form the second half of P
-      if (!mbar_wait_warp(&sm.bar_p_half, j & 1, ab)) break;
-      if (!mbar_wait_warp(&sm.bar_v[st], v_phase[st], ab)) break;
-      v_pending[st] = false;
-      v_phase[st] ^= 1;
+    issue_s(q_sa, smem_u32(sm.k[h]), tmem + HB * h, id_s);
+    mma_commit(&sm.bar_s_full[h]);
+  }
+  for (int h = 0; good && h < nh; ++h) {
+    const int r = h % NREG, st = h % KSTAGES;
+    if (!mbar_wait_warp(&sm.bar_p_ready[r], (h / NREG) & 1, ab)) break;
+    if (!mbar_wait_warp(&sm.bar_v[st], v_phase[st], ab)) break;
+    v_pending[st] = false;
+    v_phase[st] ^= 1;
+    tc_fence_after();
+    issue_pv(o_tmem, tmem + HB * r, smem_u32(sm.v[st]), id_o, h > 0);
+    mma_commit(&sm.bar_pv_done[h & 1]);
+    mma_commit(&sm.bar_kv_free[st]);
+    const int hn = h + NREG;
+    if (hn < nh) {
+      const int sn = hn % KSTAGES;
+      if (!mbar_wait_warp(&sm.bar_k[sn], k_phase[sn], ab)) break;
+      k_pending[sn] = false;
+      k_phase[sn] ^= 1;
       tc_fence_after();
-      issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 0, j > 0);
-      if (!mbar_wait_warp(&sm.bar_p_ready, j & 1, ab)) break;
-      tc_fence_after();
-      issue_pv_half(o_tmem, tmem, smem_u32(sm.v[st]), id_o, 1, true);
-      mma_commit(&sm.bar_kv_free[st]);
-      if (j + 1 < n_tiles) {
-        const int st1 = (j + 1) % STAGES;
-        if (!mbar_wait_warp(&sm.bar_k[st1], k_phase[st1], ab)) break;
-        k_pending[st1] = false;
-        k_phase[st1] ^= 1;
-        tc_fence_after();
-        issue_s(q_sa, smem_u32(sm.k[st1]), s_tmem, id_s);
-        mma_commit(&sm.bar_s_full);
-      }
-      if (j + STAGES < n_tiles) {
-        // stage st is free once S(j) and PV(j) have consumed it
-        if (!mbar_wait_warp(&sm.bar_kv_free[st], (j / STAGES) & 1, ab)) break;
-        const int t = j + STAGES;
-        mbar_arrive_expect_tx(&sm.bar_k[st], TILE_BYTES);
-        tma_load_3d(sm.k[st], tk, &sm.bar_k[st], 0, t * BN, bh);
-        mbar_arrive_expect_tx(&sm.bar_v[st], TILE_BYTES);
-        tma_load_3d(sm.v[st], tv, &sm.bar_v[st], 0, t * BN - 1, bh);
-        k_pending[st] = v_pending[st] = true;
-      }
+      issue_s(q_sa, smem_u32(sm.k[sn]), tmem + HB * r, id_s);
+      mma_commit(&sm.bar_s_full[r]);
+    }
+    const int hr = h + KSTAGES;
+    if (hr < nh) {
+      if (!mbar_wait_warp(&sm.bar_kv_free[st], (h / KSTAGES) & 1, ab)) break;
+      mbar_arrive_expect_tx(&sm.bar_k[st], HALF_BYTES);
+      tma_load_3d(sm.k[st], tk, &sm.bar_k[st], 0, hr * HB, bh);
+      mbar_arrive_expect_tx(&sm.bar_v[st], HALF_BYTES);
+      tma_load_3d(sm.v[st], tv, &sm.bar_v[st], 0, hr * HB - 1, bh);
+      k_pending[st] = v_pending[st] = true;
     }
   }
   // completion of every MMA issued so far (also the epilogue's "O ready" signal)
@@ -162,21 +173,19 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   int dummy_abort = 0;
   volatile int* nab = &dummy_abort;
   if (q_pending) mbar_wait_warp(&sm.bar_q, 0, nab);
-  for (int s = 0; s < STAGES; ++s) {
-    if (k_pending[s]) mbar_wait_warp(&sm.bar_k[s], k_phase[s], nab);
-    if (v_pending[s]) mbar_wait_warp(&sm.bar_v[s], v_phase[s], nab);
+  for (int s2 = 0; s2 < KSTAGES; ++s2) {
+    if (k_pending[s2]) mbar_wait_warp(&sm.bar_k[s2], k_phase[s2], nab);
+    if (v_pending[s2]) mbar_wait_warp(&sm.bar_v[s2], v_phase[s2], nab);
   }
-  (void)mma_issued;
   mbar_wait_warp(&sm.bar_o_done, 0, nab);
 }
 
-// P for 16 keys of one row: keys j0-1+c for c = 16*ch .. 16*ch+15 (P column c).
-// kEdge = the tile is the first key tile or the diagonal one (masking, caps);
-// interior tiles have every key visible and no caps.
+// P for 16 keys of one row: keys j0-1+c for c = 16*ch .. 16*ch+15 (P column c of
+// the half-tile starting at key j0); nvis = number of visible S columns of the row.
+// kEdge: masking and caps (first half-tile, diagonal); interior chunks use fwd_chunk_fast.
 template <bool kBF16, bool kEdge>
 __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, float scale, float m2, int nvis, int j0,
-                                          int i, float& sa, float& ea, float& bprev, float& z, uint32_t t_hi,
-                                          uint32_t t_lo) {
+                                          int i, float& sa, float& ea, float& bprev, float& z, uint32_t t_p) {
   uint32_t hi[8], lo[8];
 #pragma unroll
   for (int x = 0; x < 16; x += 2) {
@@ -199,7 +208,9 @@ __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, flo
       }
       float p = bprev + (M0 - M1);
       z += M0;
-      if (kEdge && c >= 1) {
+      if (kEdge) {
+        // column 0 holds key j0-1: with 64-key half-tiles that is row i's own key
+        // for i = q0+63 (for j0 = 0 it is key -1, and ea = 0 there)
         const int key = j0 - 1 + c;
         const float cap = 0.5f * ea * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
         p += cap;
@@ -223,8 +234,8 @@ __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, flo
     hi[x / 2] = h2;
     lo[x / 2] = kBF16 ? pack_bf16x2(pv[0] - h0, pv[1] - h1) : pack_f16x2(pv[0] - h0, pv[1] - h1);
   }
-  tmem_st8(t_hi + 8 * ch, hi);
-  tmem_st8(t_lo + 8 * ch, lo);
+  tmem_st8(t_p + 16 * ch, hi);       // P hi and lo of these 16 keys replace their own S columns
+  tmem_st8(t_p + 16 * ch + 8, lo);
 }
 
 // Interior chunk (every key visible, no caps) in packed fp32 pairs: lanes x/y
@@ -235,8 +246,7 @@ __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, flo
 // series constants carry the alternating signs.
 template <bool kBF16>
 __device__ __forceinline__ void fwd_chunk_fast(const uint32_t (&cur)[16], int ch, float2 scale2, float2 nm2,
-                                               float& sa, float& ea, float& bprev, float2& z2, uint32_t t_hi,
-                                               uint32_t t_lo) {
+                                               float& sa, float& ea, float& bprev, float2& z2, uint32_t t_p) {
   const float2 l2e = splat2(kLog2e), neg1 = splat2(-1.f);
   uint32_t hi[8], lo[8];
 #pragma unroll
@@ -275,40 +285,39 @@ __device__ __forceinline__ void fwd_chunk_fast(const uint32_t (&cur)[16], int ch
     hi[x] = h2;
     lo[x] = kBF16 ? pack_bf16x2(pv0 - h0, pv1 - h1) : pack_f16x2(pv0 - h0, pv1 - h1);
   }
-  tmem_st8(t_hi + 8 * ch, hi);
-  tmem_st8(t_lo + 8 * ch, lo);
+  tmem_st8(t_p + 16 * ch, hi);       // P hi and lo of these 16 keys replace their own S columns
+  tmem_st8(t_p + 16 * ch + 8, lo);
 }
 
 // A chunk past every row's diagonal: all weights are zero.
-__device__ __forceinline__ void fwd_chunk_zero(int ch, float& ea, float& bprev, uint32_t t_hi, uint32_t t_lo) {
+__device__ __forceinline__ void fwd_chunk_zero(int ch, float& ea, float& bprev, uint32_t t_p) {
   uint32_t zz[8];
 #pragma unroll
   for (int x = 0; x < 8; ++x) zz[x] = 0u;
-  tmem_st8(t_hi + 8 * ch, zz);
-  tmem_st8(t_lo + 8 * ch, zz);
+  tmem_st8(t_p + 16 * ch, zz);
+  tmem_st8(t_p + 16 * ch + 8, zz);
   ea = 0.f;
   bprev = 0.f;
 }
 
-// Which path chunk ch of this warp's rows takes: 0 = all zero, 1 = interior,
-// 2 = edge (masking and caps).  P column c of key tile j0 holds key j0+c-1 and
-// closes the segment into key j0+c.  On the diagonal tile (j0 = q0) the warp's
-// rows are i = q0+32w .. q0+32w+31: every segment of chunk ch is visible to all
-// of them, with no cap, when 16ch+15 <= 32w (ch < 2w); a row's last nonzero
-// column is i-j0+1 (its own key, half cap), so the chunk is zero for every row
-// when 16ch > 32w+32.  Chunk 0 of key tile 0 holds key 0 (cap) and the empty
-// segment before it.
-__device__ __forceinline__ int fwd_chunk_kind(int ch, int warp, bool diag, bool first) {
-  if (first && ch == 0) return 2;
+// Which path chunk ch (keys kb-1+16ch .. kb+14+16ch) of half-tile kb takes for
+// this warp's rows i = q0+32w .. q0+32w+31: 0 = all zero, 1 = interior, 2 = edge
+// (masking and caps).  Outside the two diagonal half-tiles every key is visible.
+// On them, every segment of the chunk is visible to all the warp's rows, with no
+// cap, when kb+16ch+15 <= q0+32w; a row's last nonzero P column holds its own key
+// (half cap), so the chunk is zero for every row when kb+16ch-1 > q0+32w+31.
+// Chunk 0 of half-tile 0 holds key 0 (cap) and the empty segment before it.
+__device__ __forceinline__ int fwd_chunk_kind(int ch, int kb, int q0, int warp, bool diag) {
+  if (kb == 0 && ch == 0) return 2;
   if (!diag) return 1;
-  if (ch < 2 * warp) return 1;
-  if (16 * ch > 32 * warp + 32) return 0;
+  if (kb + 16 * ch + 15 <= q0 + 32 * warp) return 1;
+  if (kb + 16 * ch - 1 > q0 + 32 * warp + 31) return 0;
   return 2;
 }
 
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32, float* stats,
-                           int bh, int h, int Tn, int q0, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
+                           int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = warp * 32 + lane;
@@ -316,45 +325,50 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   const bool row_ok = i < Tn;
   const float scale = expf(log_gain[h]) * inv_sqrt_d;
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const uint32_t tS = tmem + TMEM_S + lane_base;
   const uint32_t tO = tmem + TMEM_O + lane_base;
 
   float m_used = -INFINITY, z = 0.f, bpend = 0.f, sprev = 0.f;
   float2 z2 = splat2(0.f);   // packed partial of z from interior chunks
   const float2 scale2 = splat2(scale);
   bool ok = true;
-  for (int j = 0; j < n_tiles; ++j) {
-    const bool got = mbar_wait(&sm.bar_s_full, j & 1, ab);
+  for (int hh = 0; hh < nh; ++hh) {
+    const int reg = hh % NREG;
+    const bool got = mbar_wait(&sm.bar_s_full[reg], (hh / NREG) & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
-    const int j0 = j * BN;
-    const bool diag = (j == n_tiles - 1);
-    const int nvis = diag ? min(i - j0 + 1, BN) : BN;
-    // pass 1: tile max over the visible keys
+    const uint32_t tS = tmem + HB * reg + lane_base;
+    const int kb = hh * HB;                     // first key of this half-tile
+    const bool diag = hh >= nh - 2;             // the two half-tiles the diagonal crosses
+    const int nvis = diag ? min(i - kb + 1, HB) : HB;
+    // pass 1: half-tile max over the visible keys
     uint32_t sr[2][32];
     float tmax = -INFINITY;
+    tmem_ld32(tS, sr[0]);
+    tmem_ld32(tS + 32, sr[1]);
+    tmem_ld_wait();
 #pragma unroll
-    for (int c = 0; c < 4; c += 2) {
-      tmem_ld32(tS + 32 * c, sr[0]);
-      tmem_ld32(tS + 32 * (c + 1), sr[1]);
-      tmem_ld_wait();
+    for (int c2 = 0; c2 < 2; ++c2) {
+      if (diag) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        if (diag) {
+        for (int x = 0; x < 32; ++x)
+          if (32 * c2 + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[c2][x]));
+      } else {
 #pragma unroll
-          for (int x = 0; x < 32; ++x)
-            if (32 * (c + hh) + x < nvis) tmax = fmaxf(tmax, __uint_as_float(sr[hh][x]));
-        } else {
-#pragma unroll
-          for (int x = 0; x < 32; ++x) tmax = fmaxf(tmax, __uint_as_float(sr[hh][x]));
-        }
+        for (int x = 0; x < 32; ++x) tmax = fmaxf(tmax, __uint_as_float(sr[c2][x]));
       }
     }
     tmax *= scale;
     const bool need = tmax > m_used + kRescaleNats;
-    if (j == 0) {
+    if (hh == 0) {
       m_used = tmax;
     } else if (__any_sync(0xffffffffu, need)) {
+      // O holds P V' of every earlier half-tile: wait until the last of them has
+      // landed (its commit covers every MMA issued before it).  The barrier of
+      // half-tile hh-1 cannot be a phase further on (that needs P_{hh+1}) nor a
+      // phase behind (P V'_{hh-3} completed before S_hh), so its parity is exact.
+      const bool got2 = mbar_wait(&sm.bar_pv_done[(hh - 1) & 1], ((hh - 1) >> 1) & 1, ab);
+      if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
+      tc_fence_after();
       const float m_new = need ? tmax : m_used;
       const float alpha = exp_rel(m_used - m_new);
       z *= alpha;
@@ -369,40 +383,35 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
         for (int x = 0; x < 32; ++x) sr[1][x] = __float_as_uint(__uint_as_float(sr[1][x]) * alpha);
         tmem_st32(tO + 32 * half, sr[1]);
       }
+      tmem_st_wait();
     }
     const float m2 = m_used * kLog2e;
     float sa = sprev;
-    float ea = (j0 > 0) ? ex2_approx(fmaf(sprev, kLog2e, -m2)) : 0.f;
+    float ea = (kb > 0) ? ex2_approx(fmaf(sprev, kLog2e, -m2)) : 0.f;
     float bprev = bpend;
     // pass 2: P for 16 keys at a time; the next chunk's load overlaps this chunk's math
-    const uint32_t t_lo = tmem + TMEM_PLO + lane_base;
     const float2 nm2 = splat2(-m2);
     uint32_t bufA[16], bufB[16];
     tmem_ld16(tS, bufA);
     tmem_ld_wait();
 #define CA_FWD_CHUNK(BUF, CH)                                                                    \
   {                                                                                              \
-    const int kind = fwd_chunk_kind(CH, warp, diag, j == 0);                                     \
-    if (kind == 1) fwd_chunk_fast<kBF16>(BUF, CH, scale2, nm2, sa, ea, bprev, z2, tS, t_lo);     \
-    else if (kind == 2) fwd_chunk<kBF16, true>(BUF, CH, scale, m2, nvis, j0, i, sa, ea, bprev, z, tS, t_lo); \
-    else fwd_chunk_zero(CH, ea, bprev, tS, t_lo);                                                \
+    const int kind = fwd_chunk_kind(CH, kb, q0, warp, diag);                                     \
+    if (kind == 1) fwd_chunk_fast<kBF16>(BUF, CH, scale2, nm2, sa, ea, bprev, z2, tS);           \
+    else if (kind == 2) fwd_chunk<kBF16, true>(BUF, CH, scale, m2, nvis, kb, i, sa, ea, bprev, z, tS); \
+    else fwd_chunk_zero(CH, ea, bprev, tS);                                                      \
   }
 #pragma unroll 1
-    for (int ch = 0; ch < 8; ch += 2) {
+    for (int ch = 0; ch < HB / 16; ch += 2) {
       tmem_ld16(tS + 16 * (ch + 1), bufB);
       CA_FWD_CHUNK(bufA, ch);
       tmem_ld_wait();
-      if (ch + 2 < 8) tmem_ld16(tS + 16 * (ch + 2), bufA);
+      if (ch + 2 < HB / 16) tmem_ld16(tS + 16 * (ch + 2), bufA);
       CA_FWD_CHUNK(bufB, ch + 1);
       tmem_ld_wait();
-      if (ch == 2) {   // P of keys 0..63 complete: the producer starts its half of P V'
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&sm.bar_p_half);
-      }
     }
 #undef CA_FWD_CHUNK
-    if (diag && i == j0 + BN - 1) {   // cap of key i sits in the last column: keep it pending
+    if (hh == nh - 1 && i == kb + HB - 1) {   // key i is the last key: its cap stays pending
       bprev += 0.5f * ea;
       z += 0.5f * ea;
     }
@@ -410,7 +419,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     sprev = sa;
     tmem_st_wait();
     tc_fence_before();
-    mbar_arrive(&sm.bar_p_ready);
+    mbar_arrive(&sm.bar_p_ready[reg]);
   }
 
   if (ok) ok = mbar_wait(&sm.bar_o_done, 0, ab);
@@ -473,19 +482,22 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const int bh = blockIdx.x % BH;
   const int qt = nqt - 1 - blockIdx.x / BH;   // heaviest query tiles first
   const int q0 = qt * BM;
-  const int n_tiles = qt + 1;                 // key tiles 0..qt (BN == BM)
+  const int nh = 2 * (qt + 1);                // key half-tiles 0 .. 2qt+1 (keys 0 .. q0+127)
 
   if (warp == 4) {
     if (lane == 0) {
       mbar_init(&sm.bar_q, 1);
-      for (int s = 0; s < STAGES; ++s) {
+      for (int s = 0; s < KSTAGES; ++s) {
         mbar_init(&sm.bar_k[s], 1);
         mbar_init(&sm.bar_v[s], 1);
         mbar_init(&sm.bar_kv_free[s], 1);
       }
-      mbar_init(&sm.bar_s_full, 1);
-      mbar_init(&sm.bar_p_half, 128);
-      mbar_init(&sm.bar_p_ready, 128);
+      for (int g = 0; g < NREG; ++g) {
+        mbar_init(&sm.bar_s_full[g], 1);
+        mbar_init(&sm.bar_p_ready[g], 128);
+      }
+      mbar_init(&sm.bar_pv_done[0], 1);
+      mbar_init(&sm.bar_pv_done[1], 1);
       mbar_init(&sm.bar_o_done, 1);
       sm.abort_flag = 0;
       fence_mbar_init();
@@ -503,10 +515,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 4) {
-    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, n_tiles, tmem);   // whole warp, converged
+    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, n_tiles, tmem, inv_sqrt_d);
+    math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d);
   }
   tc_fence_before();
   __syncthreads();
@@ -1173,8 +1185,8 @@ template <bool kBF16>
 static cudaError_t launch_fwd(const FwdArgs& a) {
   const long long BH = a.B * a.H;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16) || !make_map(&mk, a.k, BH, a.T, a.D, kBF16) ||
-      !make_map(&mv, a.v, BH, a.T, a.D, kBF16))
+  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, fwd::BM) || !make_map(&mk, a.k, BH, a.T, a.D, kBF16, fwd::HB) ||
+      !make_map(&mv, a.v, BH, a.T, a.D, kBF16, fwd::HB))
     return cudaErrorInvalidValue;
   auto kern = fwd::fwd_kernel<kBF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd::kSmemBytes);
