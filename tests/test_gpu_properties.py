@@ -187,3 +187,31 @@ def test_bounded_wait_timeout_is_reported_and_context_survives():
     y2 = ca.continuum_attention(q, k, v, lg)
     assert torch.isfinite(y1.float()).all() and torch.equal(y1, y2)
     assert lib.ca_device_status(0) == 0
+
+
+@pytest.mark.parametrize("T", [16384, 32768])
+def test_long_context_rows_and_identities(T):
+    # BASELINE config 3 lengths: sampled query rows (including the last) against the
+    # float64 oracle on the full causal prefix, plus the exact gradient identities
+    from oracle.ca_oracle import ca_weights_tile
+    H = 4
+    q, k, v, dy = (t.to(DEV, torch.bfloat16) for t in gen_inputs((1, H, T, 64), 41, qk_mag=2.0, dup_frac=0.1))
+    lg = torch.linspace(-0.2, 0.3, H, device=DEV)
+    y, gq, gk, gv, gg = _op_grads(q, k, v, lg, dy)
+    assert torch.isfinite(y.float()).all() and torch.isfinite(gq.float()).all()
+    rows = [0, 1, 63, 64, 127, 128, T // 2 + 5, T - 129, T - 65, T - 1]
+    qd, kd, vd = (t[0].double().cpu() for t in (q, k, v))
+    for h in range(H):
+        scale = math.exp(float(lg[h])) / 8.0
+        for i in rows:
+            s = (qd[h, i:i + 1] @ kd[h, :i + 1].T) * scale          # [1, i+1]
+            w = ca_weights_tile(s.unsqueeze(0), i)[0]                # row i's weights over keys 0..i
+            ref = w @ vd[h, :i + 1]
+            err = (y[0, h, i].double().cpu() - ref[0]).abs().max().item()
+            assert err <= 4e-3 * ref.abs().max().item() + 4e-3, (h, i, err)
+    sv, so = gv.double().sum(2), dy.double().sum(2)
+    assert norm_max_err(sv, so) < 2e-2
+    via_q = (gq.double() * q.double()).sum(dim=(0, 2, 3))
+    via_k = (gk.double() * k.double()).sum(dim=(0, 2, 3))
+    assert norm_max_err(via_q, gg.double()) < 2e-2
+    assert norm_max_err(via_k, gg.double()) < 2e-2
