@@ -48,6 +48,14 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
+// Programmatic dependent launch: every kernel of this library is launched so that
+// it may start while the previous kernel in the stream is finishing.  pdl_wait()
+// blocks until that kernel has completed and its writes are visible (at once when
+// there is no such kernel), so it precedes every global-memory access;
+// pdl_launch_dependents() allows the next kernel to begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // e^x for x <= 0 relative to a row max (x = -inf gives 0).
 __device__ __forceinline__ float exp_rel(float x) { return ex2_approx(x * kLog2e); }
 

@@ -49,6 +49,24 @@ struct BwdWorkspace {
   int nparts;
 };
 
+// Launch with programmatic stream serialisation (the kernel calls pdl_wait()
+// before its first global-memory access).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 namespace simt {
 constexpr int kForwardLaunches = 1;
 inline int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ cast (+ d log_gain)

@@ -70,6 +70,8 @@ __device__ __forceinline__ void store8<__half>(__half* p, const float (&x)[8]) {
 template <typename T>
 __global__ void pack_fwd_kernel(const T* __restrict__ qkv, const float2* __restrict__ cs, T* __restrict__ q,
                                 T* __restrict__ k, T* __restrict__ v, int Tn, int H, int D, size_t total) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int chunks = D / 8;
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -104,6 +106,8 @@ template <typename T>
 __global__ void pack_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv,
                                 const float2* __restrict__ cs, T* __restrict__ dqkv, int Tn, int H, int D,
                                 size_t total) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int chunks = D / 8;
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -142,18 +146,16 @@ template <typename T>
 static cudaError_t fwd_t(const void* qkv, const float* cs, void* q, void* k, void* v, long long B, long long Tn,
                          long long H, long long D, cudaStream_t s) {
   const size_t total = (size_t)B * Tn * 3 * H * (D / 8);
-  pack_fwd_kernel<T><<<grid_for(total), 256, 0, s>>>((const T*)qkv, (const float2*)cs, (T*)q, (T*)k, (T*)v,
-                                                     (int)Tn, (int)H, (int)D, total);
-  return cudaGetLastError();
+  return launch_pdl(pack_fwd_kernel<T>, dim3(grid_for(total)), dim3(256), 0, s, (const T*)qkv,
+                    (const float2*)cs, (T*)q, (T*)k, (T*)v, (int)Tn, (int)H, (int)D, total);
 }
 
 template <typename T>
 static cudaError_t bwd_t(const void* dq, const void* dk, const void* dv, const float* cs, void* dqkv, long long B,
                          long long Tn, long long H, long long D, cudaStream_t s) {
   const size_t total = (size_t)B * Tn * 3 * H * (D / 8);
-  pack_bwd_kernel<T><<<grid_for(total), 256, 0, s>>>((const T*)dq, (const T*)dk, (const T*)dv, (const float2*)cs,
-                                                     (T*)dqkv, (int)Tn, (int)H, (int)D, total);
-  return cudaGetLastError();
+  return launch_pdl(pack_bwd_kernel<T>, dim3(grid_for(total)), dim3(256), 0, s, (const T*)dq, (const T*)dk,
+                    (const T*)dv, (const float2*)cs, (T*)dqkv, (int)Tn, (int)H, (int)D, total);
 }
 
 cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, long long B, long long T,

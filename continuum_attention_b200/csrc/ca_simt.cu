@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(NT)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const float* __restrict__ log_gain, T* __restrict__ o, float* __restrict__ o32,
            float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d) {
+  pdl_wait();
+  pdl_launch_dependents();
   using L = FwdSmem<DP>;
   constexpr int DQ = DP / 4;             // O columns per thread
   extern __shared__ float smem[];
@@ -255,6 +257,8 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            float* __restrict__ dq_acc, T* __restrict__ dk, T* __restrict__ dv,
            float* __restrict__ gain_part, int BH, int H, int Tn, int D, float inv_sqrt_d) {
+  pdl_wait();
+  pdl_launch_dependents();
   using L = BwdSmem<DP>;
   constexpr int DQ = DP / 4;
   extern __shared__ float smem[];
@@ -485,6 +489,8 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 template <typename TO, typename T>
 __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ dout,
                               float* __restrict__ rowdot, size_t rows, int D) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t row = (size_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -500,6 +506,8 @@ __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ do
 template <typename TO, typename T>
 __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ dout, float* __restrict__ rowdot,
                               float* __restrict__ dq_acc, size_t rows) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const size_t row = gid >> 4;
   const int part = (int)(gid & 15);
@@ -560,6 +568,8 @@ template <typename T, bool kVec>
 __global__ void cast_gain_kernel(const float* __restrict__ src, T* __restrict__ dst, size_t n, int cast_blocks,
                                  const float* __restrict__ part, float* __restrict__ gout, int B, int H,
                                  int nparts) {
+  pdl_wait();
+  pdl_launch_dependents();
   if ((int)blockIdx.x >= cast_blocks) {
     gain_reduce_block(part, gout, B, H, nparts, (int)blockIdx.x - cast_blocks);
     return;
@@ -592,10 +602,9 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   if (e != cudaSuccess) return e;
   const long long BH = a.B * a.H;
   const long long nqt = (a.T + BQ - 1) / BQ;
-  kern<<<dim3((unsigned)(BH * nqt)), NT, smem, a.stream>>>(
-      (const T*)a.q, (const T*)a.k, (const T*)a.v, a.log_gain, (T*)a.o, a.o_f32, a.row_stats,
-      (int)BH, (int)a.H, (int)a.T, (int)a.D, a.inv_sqrt_d);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
+                    (const T*)a.v, a.log_gain, (T*)a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T,
+                    (int)a.D, a.inv_sqrt_d);
 }
 
 template <typename T>
@@ -621,23 +630,21 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   if (e != cudaSuccess) return e;
   const long long BH = a.B * a.H;
   const long long nkt = (a.T + BK - 1) / BK;
-  kern<<<dim3((unsigned)(BH * nkt)), NT, smem, a.stream>>>(
-      (const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)a.d_o, a.log_gain, a.row_stats,
-      w.rowdot, w.dq_acc, (T*)a.dk, (T*)a.dv, a.dlog_gain ? w.gain_part : nullptr, (int)BH,
-      (int)a.H, (int)a.T, (int)a.D, a.inv_sqrt_d);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3((unsigned)(BH * nkt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
+                    (const T*)a.v, (const T*)a.d_o, a.log_gain, a.row_stats, (const float*)w.rowdot, w.dq_acc,
+                    (T*)a.dk, (T*)a.dv, a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T,
+                    (int)a.D, a.inv_sqrt_d);
 }
 
 template <typename T>
 static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
   const size_t rows = (size_t)a.B * a.H * a.T;
+  const dim3 grid((unsigned)((rows + 7) / 8));
   if (a.o_f32)
-    rowdot_kernel<float, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o, rowdot,
-                                                                              rows, (int)a.D);
-  else
-    rowdot_kernel<T, T><<<(unsigned)((rows + 7) / 8), 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o, rowdot,
-                                                                          rows, (int)a.D);
-  return cudaGetLastError();
+    return launch_pdl(rowdot_kernel<float, T>, grid, dim3(256), 0, a.stream, (const float*)a.o_f32,
+                      (const T*)a.d_o, rowdot, rows, (int)a.D);
+  return launch_pdl(rowdot_kernel<T, T>, grid, dim3(256), 0, a.stream, (const T*)a.o, (const T*)a.d_o, rowdot,
+                    rows, (int)a.D);
 }
 
 template <typename T>
@@ -653,10 +660,10 @@ static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc) {
   }
   const unsigned blocks = (unsigned)((rows * 16 + 255) / 256);
   if (a.o_f32)
-    prep64_kernel<float, T><<<blocks, 256, 0, a.stream>>>(a.o_f32, (const T*)a.d_o, rowdot, dq_acc, rows);
-  else
-    prep64_kernel<T, T><<<blocks, 256, 0, a.stream>>>((const T*)a.o, (const T*)a.d_o, rowdot, dq_acc, rows);
-  return cudaGetLastError();
+    return launch_pdl(prep64_kernel<float, T>, dim3(blocks), dim3(256), 0, a.stream, (const float*)a.o_f32,
+                      (const T*)a.d_o, rowdot, dq_acc, rows);
+  return launch_pdl(prep64_kernel<T, T>, dim3(blocks), dim3(256), 0, a.stream, (const T*)a.o, (const T*)a.d_o,
+                    rowdot, dq_acc, rows);
 }
 
 cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc) {
@@ -675,12 +682,10 @@ static cudaError_t cast_dtype(const BwdArgs& a, const float* dq_acc, const float
   const int cast_blocks = (int)std::min<size_t>(std::max<size_t>((items + 255) / 256, 1), 148 * 16);
   const unsigned blocks = (unsigned)(cast_blocks + (a.dlog_gain ? a.H : 0));
   if (vec)
-    cast_gain_kernel<T, true><<<blocks, 256, 0, a.stream>>>(dq_acc, (T*)a.dq, n, cast_blocks, part, a.dlog_gain,
-                                                           (int)a.B, (int)a.H, nparts);
-  else
-    cast_gain_kernel<T, false><<<blocks, 256, 0, a.stream>>>(dq_acc, (T*)a.dq, n, cast_blocks, part, a.dlog_gain,
-                                                            (int)a.B, (int)a.H, nparts);
-  return cudaGetLastError();
+    return launch_pdl(cast_gain_kernel<T, true>, dim3(blocks), dim3(256), 0, a.stream, dq_acc, (T*)a.dq, n,
+                      cast_blocks, part, a.dlog_gain, (int)a.B, (int)a.H, nparts);
+  return launch_pdl(cast_gain_kernel<T, false>, dim3(blocks), dim3(256), 0, a.stream, dq_acc, (T*)a.dq, n,
+                    cast_blocks, part, a.dlog_gain, (int)a.B, (int)a.H, nparts);
 }
 
 cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* gain_part, int nparts) {

@@ -513,6 +513,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // the set-up above touches no global data; everything below may read or write
+  // what the previous kernel in the stream produced or consumed
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 4) {
     producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
@@ -1102,6 +1106,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // the set-up above touches no global data; everything below may read or write
+  // what the previous kernel in the stream produced or consumed
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == NUM_MATH_WARPS) {
     producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, bh, j0, n_tiles, tmem);   // whole warp, converged
@@ -1192,9 +1200,8 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nqt = (a.T + fwd::BM - 1) / fwd::BM;
-  kern<<<dim3((unsigned)(BH * nqt)), fwd::NUM_THREADS, fwd::kSmemBytes, a.stream>>>(
-      mq, mk, mv, a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(fwd::NUM_THREADS), fwd::kSmemBytes, a.stream, mq, mk, mv,
+                    a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
 }
 
 cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a) : launch_fwd<false>(a); }
@@ -1213,10 +1220,9 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;
-  kern<<<dim3((unsigned)(BH * nkt)), bwd::NUM_THREADS, bwd::kSmemBytes, a.stream>>>(
-      mq, mk, mv, mdo, mdq, a.log_gain, a.row_stats, w.rowdot, a.dk, a.dv,
-      a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3((unsigned)(BH * nkt)), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo,
+                 mdq, a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv,
+                 a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
   if (e != cudaSuccess) return e;
   return simt::launch_cast_dq(a, w.dq_acc, w.gain_part, (int)nkt);
 }
