@@ -45,7 +45,7 @@ constexpr long long kMinKeyTile = 64;  // smallest key tile of any backward kern
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct Layout {
-  size_t rowdot, dq_acc, gain_part, total;
+  size_t rowdot, dq_acc, gain_part, counter, total;
   int nparts;
 };
 
@@ -56,7 +56,8 @@ Layout workspace_layout(long long B, long long H, long long T, long long D) {
   l.rowdot = 0;
   l.dq_acc = align_up(l.rowdot + rows * sizeof(float));
   l.gain_part = align_up(l.dq_acc + rows * (size_t)D * sizeof(float));
-  l.total = align_up(l.gain_part + (size_t)B * H * l.nparts * sizeof(float));
+  l.counter = align_up(l.gain_part + (size_t)B * H * l.nparts * sizeof(float));
+  l.total = align_up(l.counter + sizeof(unsigned));
   return l;
 }
 
@@ -148,7 +149,7 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
     return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: workspace must be %zu-byte aligned", kAlign);
   char* ws = (char*)workspace;
   ca::BwdWorkspace w{(float*)(ws + l.rowdot), (float*)(ws + l.dq_acc), (float*)(ws + l.gain_part),
-                     l.nparts};
+                     l.nparts, (unsigned*)(ws + l.counter)};
   ca::BwdArgs a{q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
                 (float)(1.0 / std::sqrt((double)D)), s};
   cudaError_t e;

@@ -47,6 +47,7 @@ struct BwdWorkspace {
   float* dq_acc;     // [B*H*T*D]    fp32 dQ accumulator
   float* gain_part;  // [B*H*nparts] per-(head, key tile) partial sums of dS*s
   int nparts;
+  unsigned* counter; // work-item counter of the persistent tcgen05 backward (zeroed by prep)
 };
 
 // Launch with programmatic stream serialisation (the kernel calls pdl_wait()
@@ -73,7 +74,8 @@ inline int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ
 cudaError_t forward(const FwdArgs& a);
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
 // backward helpers shared with the tcgen05 path
-cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc);  // D_i = dO_i . O_i, dq_acc = 0
+// D_i = dO_i . O_i, dq_acc = 0, *counter = 0 (when counter != nullptr)
+cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter);
 // fp32 dQ -> dtype, and (when a.dlog_gain) d log_gain from the per-key-tile partials, one launch
 cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* gain_part, int nparts);
 }  // namespace simt

@@ -505,10 +505,11 @@ __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ do
 // (16-byte O loads when O is fp32, 8-byte dO loads), 2 rows per warp.
 template <typename TO, typename T>
 __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ dout, float* __restrict__ rowdot,
-                              float* __restrict__ dq_acc, size_t rows) {
+                              float* __restrict__ dq_acc, size_t rows, unsigned* __restrict__ counter) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid == 0 && counter) *counter = 0u;   // work-item counter of the persistent backward
   const size_t row = gid >> 4;
   const int part = (int)(gid & 15);
   float s = 0.f;
@@ -648,7 +649,7 @@ static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
 }
 
 template <typename T>
-static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc) {
+static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter) {
   const size_t rows = (size_t)a.B * a.H * a.T;
   const uintptr_t oal = reinterpret_cast<uintptr_t>(a.o_f32 ? (const void*)a.o_f32 : a.o);
   const bool vec = a.D == 64 && (reinterpret_cast<uintptr_t>(a.d_o) & (4 * sizeof(T) - 1)) == 0 &&
@@ -656,21 +657,25 @@ static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc) {
   if (!vec) {
     cudaError_t e = rowdot_dtype<T>(a, rowdot);
     if (e != cudaSuccess) return e;
+    if (counter) {
+      e = cudaMemsetAsync(counter, 0, sizeof(unsigned), a.stream);
+      if (e != cudaSuccess) return e;
+    }
     return cudaMemsetAsync(dq_acc, 0, rows * a.D * sizeof(float), a.stream);
   }
   const unsigned blocks = (unsigned)((rows * 16 + 255) / 256);
   if (a.o_f32)
     return launch_pdl(prep64_kernel<float, T>, dim3(blocks), dim3(256), 0, a.stream, (const float*)a.o_f32,
-                      (const T*)a.d_o, rowdot, dq_acc, rows);
+                      (const T*)a.d_o, rowdot, dq_acc, rows, counter);
   return launch_pdl(prep64_kernel<T, T>, dim3(blocks), dim3(256), 0, a.stream, (const T*)a.o, (const T*)a.d_o,
-                    rowdot, dq_acc, rows);
+                    rowdot, dq_acc, rows, counter);
 }
 
-cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc) {
+cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter) {
   switch (a.dtype) {
-    case 0: return prep_dtype<float>(a, rowdot, dq_acc);
-    case 1: return prep_dtype<__nv_bfloat16>(a, rowdot, dq_acc);
-    default: return prep_dtype<__half>(a, rowdot, dq_acc);
+    case 0: return prep_dtype<float>(a, rowdot, dq_acc, counter);
+    case 1: return prep_dtype<__nv_bfloat16>(a, rowdot, dq_acc, counter);
+    default: return prep_dtype<__half>(a, rowdot, dq_acc, counter);
   }
 }
 
@@ -698,7 +703,7 @@ cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* g
 
 template <typename T>
 static cudaError_t bwd_dtype(const BwdArgs& a, const BwdWorkspace& w) {
-  cudaError_t e = launch_prep(a, w.rowdot, w.dq_acc);
+  cudaError_t e = launch_prep(a, w.rowdot, w.dq_acc, nullptr);
   if (e != cudaSuccess) return e;
   if (a.D <= 32) e = launch_bwd<T, 32>(a, w);
   else if (a.D <= 64) e = launch_bwd<T, 64>(a, w);

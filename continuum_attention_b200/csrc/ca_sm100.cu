@@ -31,6 +31,8 @@
 // for its own in-flight copies and MMAs, frees its TMEM and returns.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "ca_common.cuh"
 #include "ca_internal.h"
 #include "ca_sm100_ptx.cuh"
@@ -589,8 +591,11 @@ struct __align__(1024) Smem {
   uint64_t bar_mma_done;
   uint64_t bar_drain;
   uint64_t bar_dq_free;              // the staged dQ tile has been read by its reduce
+  uint64_t bar_item;                 // the producer has published the next work item
   uint32_t tmem_base;
   int abort_flag;
+  int item;                          // published work item (n_items: none left)
+  int decision;                      // the item every math warp takes next
   float red[NUM_MATH_WARPS];
 };
 
@@ -637,88 +642,193 @@ __device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tme
   }
 }
 
+// Work item w (heaviest first): key tile kt = w / BH of head-sequence bh = w % BH,
+// with n = nkt - kt query tiles.
+struct Item {
+  int bh, kt, j0, n;
+};
+__device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
+  Item it;
+  it.bh = w % BH;
+  it.kt = w / BH;
+  it.j0 = it.kt * BN;
+  it.n = nkt - it.kt;
+  return it;
+}
+
+// Persistent producer: items come from a global counter (the first is blockIdx.x,
+// then gridDim.x + atomicAdd(counter)).  Barrier phases are counted in global
+// tiles g (all items of this CTA in order): s_full, s_consumed, mma_done and the
+// dQ reduces advance once per tile, p_ready once per tile plus once per item (the
+// last dQ is staged after the item's tile loop), the Q/dO ring by stage.  The next
+// item's first Q/dO tiles go into the ring as soon as this item's last tiles free
+// their stages, and its K/V once this item's last gradient MMAs complete, so its
+// start overlaps this item's epilogue.
 template <bool kBF16>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
-                         const CUtensorMap* tdo, const CUtensorMap* tdq, int bh, int j0, int n_tiles,
-                         uint32_t tmem) {
+                         const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int n_items,
+                         unsigned* counter, uint32_t tmem) {
   volatile int* ab = &sm.abort_flag;
+  const int lane = threadIdx.x & 31;
   const uint32_t id_s = make_idesc(BM, KH, kBF16, false, false);
   const uint32_t id_mn = make_idesc(BN, HD, kBF16, true, true);
   const uint32_t id_dq = make_idesc(BM, HD, kBF16, true, false);
-  bool kv_pending = true;
+  bool kv_pending = false;
+  uint32_t kv_phase = 0;
   bool q_pending[QSTAGES];
   uint32_t q_phase[QSTAGES];
   for (int s2 = 0; s2 < QSTAGES; ++s2) {
     q_pending[s2] = false;
     q_phase[s2] = 0;
   }
+  auto fetch = [&]() -> int {
+    unsigned k = 0;
+    if (lane == 0) k = atomicAdd(counter, 1u);
+    k = __shfl_sync(0xffffffffu, k, 0);
+    return (int)(gridDim.x + k);
+  };
+  auto load_kv = [&](const Item& it) {
+    mbar_arrive_expect_tx(&sm.bar_kv, 2 * KV_BYTES);
+    tma_load_3d(sm.k, tk, &sm.bar_kv, 0, it.j0 - KOFF, it.bh);
+    tma_load_3d(sm.v, tv, &sm.bar_kv, 0, it.j0 - KOFF, it.bh);
+    kv_pending = true;
+  };
+  auto load_qdo = [&](int st, const Item& it, int t) {
+    mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
+    tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
+    tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
+    q_pending[st] = true;
+  };
+  auto publish = [&](int w) {
+    if (lane == 0) {
+      sm.item = w;
+      mbar_arrive(&sm.bar_item);
+    }
+    __syncwarp();
+  };
 
-  mbar_arrive_expect_tx(&sm.bar_kv, 2 * KV_BYTES);
-  tma_load_3d(sm.k, tk, &sm.bar_kv, 0, j0 - KOFF, bh);
-  tma_load_3d(sm.v, tv, &sm.bar_kv, 0, j0 - KOFF, bh);
-  for (int t = 0; t < QSTAGES && t < n_tiles; ++t) {
-    mbar_arrive_expect_tx(&sm.bar_qdo[t], 2 * QT_BYTES);
-    tma_load_3d(sm.q[t], tq, &sm.bar_qdo[t], 0, j0 + t * BM, bh);
-    tma_load_3d(sm.dout[t], tdo, &sm.bar_qdo[t], 0, j0 + t * BM, bh);
-    q_pending[t] = true;
+  int item = blockIdx.x;
+  int next = -1;         // claimed next item (-1: not claimed yet; claims happen late, see below)
+  uint32_t g0 = 0;       // global index of the current item's first tile
+  uint32_t pr = 0;       // p_ready phases consumed
+  uint32_t issued = 0;   // global tiles whose Q/dO load has been issued
+  int committed = -1;    // last global tile whose gradient MMAs were committed
+  int completed = -1;    // last global tile whose gradient MMAs are known complete
+  // Issue Q/dO loads for global tiles issued .. upto-1 that belong to the current
+  // or the next item.  Global tile x uses stage x % QSTAGES, last read by the
+  // gradient MMAs of tile x - QSTAGES; those are waited for through the most
+  // recent commit (its phase is the only open one, so the parity is exact).
+  auto ensure_loaded = [&](const Item& it, bool has_next, const Item& nx, uint32_t upto) -> bool {
+    while (issued < upto) {
+      const uint32_t x = issued;
+      const bool mine = x < g0 + it.n;
+      if (!mine && !(has_next && x < g0 + it.n + nx.n)) break;
+      if ((int)x - QSTAGES > completed) {
+        if (!mbar_wait_warp(&sm.bar_mma_done, (uint32_t)committed & 1, ab)) return false;
+        completed = committed;
+      }
+      if (mine) load_qdo((int)(x % QSTAGES), it, (int)(x - g0));
+      else load_qdo((int)(x % QSTAGES), nx, (int)(x - g0 - it.n));
+      ++issued;
+    }
+    return true;
+  };
+  bool good = item < n_items;
+  if (good) {
+    const Item it = decode_item(item, BH, nkt);
+    load_kv(it);
   }
-  if (mbar_wait_warp(&sm.bar_kv, 0, ab) && mbar_wait_warp(&sm.bar_qdo[0], 0, ab)) {
+  publish(good ? item : n_items);
+  while (good) {
+    const Item it = decode_item(item, BH, nkt);
+    // The next item is claimed as late as its first Q/dO prefetch allows (the
+    // item's second-to-last tile, or its start when it has one tile), so that the
+    // counter hands the heaviest remaining items to the CTAs that free up first.
+    bool has_next = false;
+    Item nx = decode_item(0, BH, nkt);
+    auto claim = [&]() {
+      next = fetch();
+      has_next = next < n_items;
+      if (has_next) nx = decode_item(next, BH, nkt);
+    };
+    next = -1;
+    if (it.n == 1) claim();
+    if (!ensure_loaded(it, has_next, nx, g0 + (uint32_t)min(QSTAGES, it.n))) break;
+    const int st0 = (int)(g0 % QSTAGES);
+    if (!mbar_wait_warp(&sm.bar_kv, kv_phase, ab) || !mbar_wait_warp(&sm.bar_qdo[st0], q_phase[st0], ab)) break;
     kv_pending = false;
-    q_pending[0] = false;
-    q_phase[0] ^= 1;
+    kv_phase ^= 1;
+    q_pending[st0] = false;
+    q_phase[st0] ^= 1;
     tc_fence_after();
-    issue_s_dp<kBF16>(sm, 0, tmem, id_s);
+    issue_s_dp<kBF16>(sm, st0, tmem, id_s);
     mma_commit(&sm.bar_s_full);
-    for (int t = 0; t < n_tiles; ++t) {
-      const int st = t % QSTAGES;
-      if (!mbar_wait_warp(&sm.bar_s_consumed, t & 1, ab)) break;
-      if (t + 1 < n_tiles) {
-        const int st1 = (t + 1) % QSTAGES;
-        if (!mbar_wait_warp(&sm.bar_qdo[st1], q_phase[st1], ab)) break;
+    for (int t = 0; t < it.n && good; ++t) {
+      const uint32_t g = g0 + t;
+      const int st = (int)(g % QSTAGES);
+      const bool last = t == it.n - 1;
+      if (t == it.n - 2) claim();
+      if (!mbar_wait_warp(&sm.bar_s_consumed, g & 1, ab)) { good = false; break; }
+      if (t + 1 < it.n) {
+        const int st1 = (int)((g + 1) % QSTAGES);
+        if (!mbar_wait_warp(&sm.bar_qdo[st1], q_phase[st1], ab)) { good = false; break; }
         q_pending[st1] = false;
         q_phase[st1] ^= 1;
         tc_fence_after();
         issue_s_dp<kBF16>(sm, st1, tmem, id_s);
         mma_commit(&sm.bar_s_full);
       }
-      if (!mbar_wait_warp(&sm.bar_p_ready, t & 1, ab)) break;
+      if (!mbar_wait_warp(&sm.bar_p_ready, pr & 1, ab)) { good = false; break; }
+      ++pr;
       tc_fence_after();
       issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
       mma_commit(&sm.bar_mma_done);
+      committed = (int)g;
       // the math warps staged dQ of query tile t-1 before arriving on p_ready
       if (t > 0) {
-        tma_reduce_add_3d(tdq, sm.dqs[0], 0, j0 + (t - 1) * BM, bh);
-        tma_reduce_add_3d(tdq, sm.dqs[1], 32, j0 + (t - 1) * BM, bh);
+        tma_reduce_add_3d(tdq, sm.dqs[0], 0, it.j0 + (t - 1) * BM, it.bh);
+        tma_reduce_add_3d(tdq, sm.dqs[1], 32, it.j0 + (t - 1) * BM, it.bh);
         bulk_commit_group();
       }
-      if (t + QSTAGES < n_tiles) {
-        if (!mbar_wait_warp(&sm.bar_mma_done, t & 1, ab)) break;
-        const int tt = t + QSTAGES;
-        mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
-        tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
-        tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, j0 + tt * BM, bh);
-        q_pending[st] = true;
+      // stage st takes global tile g + QSTAGES (this item's or the next item's)
+      if (!ensure_loaded(it, has_next, nx, g + QSTAGES + 1)) { good = false; break; }
+      if (last && has_next) {
+        // K' and V' are read by S/dP and by this tile's dQ MMAs: the next item's
+        // go in once the latter have completed
+        if (completed < (int)g) {
+          if (!mbar_wait_warp(&sm.bar_mma_done, g & 1, ab)) { good = false; break; }
+          completed = (int)g;
+        }
+        load_kv(nx);
       }
       if (t > 0) {
         bulk_wait_group_read0();
-        if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.bar_dq_free);
+        if (lane == 0) mbar_arrive(&sm.bar_dq_free);
         __syncwarp();
       }
-      if (t == n_tiles - 1) {
-        // the last tile's dQ is staged after the loop (p_ready phase n_tiles)
-        if (mbar_wait_warp(&sm.bar_p_ready, n_tiles & 1, ab)) {
-          tma_reduce_add_3d(tdq, sm.dqs[0], 0, j0 + t * BM, bh);
-          tma_reduce_add_3d(tdq, sm.dqs[1], 32, j0 + t * BM, bh);
-          bulk_commit_group();
-        }
+      if (last) {
+        // the item's last dQ tile is staged after its tile loop (one more p_ready phase)
+        if (!mbar_wait_warp(&sm.bar_p_ready, pr & 1, ab)) { good = false; break; }
+        ++pr;
+        tma_reduce_add_3d(tdq, sm.dqs[0], 0, it.j0 + t * BM, it.bh);
+        tma_reduce_add_3d(tdq, sm.dqs[1], 32, it.j0 + t * BM, it.bh);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        if (lane == 0) mbar_arrive(&sm.bar_dq_free);
+        __syncwarp();
       }
     }
+    if (!good) break;
+    g0 += it.n;
+    item = next;
+    good = item < n_items;
+    publish(good ? item : n_items);
   }
   // drain: every copy lands and every MMA completes before shared memory / TMEM go away
   mma_commit(&sm.bar_drain);
   int dummy = 0;
   volatile int* nab = &dummy;
-  if (kv_pending) mbar_wait_warp(&sm.bar_kv, 0, nab);
+  if (kv_pending) mbar_wait_warp(&sm.bar_kv, kv_phase, nab);
   for (int s2 = 0; s2 < QSTAGES; ++s2)
     if (q_pending[s2]) mbar_wait_warp(&sm.bar_qdo[s2], q_phase[s2], nab);
   mbar_wait_warp(&sm.bar_drain, 0, nab);
@@ -884,10 +994,12 @@ __device__ __forceinline__ void stage_dq(Smem& sm, int r, int qk, const uint32_t
   }
 }
 
+// One work item of the math warps: key tile kt of head-sequence bh, its n_tiles
+// query tiles being global tiles g0 .. g0+n_tiles-1 of this CTA.
 template <bool kBF16>
-__device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
-                           void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
-                           int kt, int nkt, int n_tiles, uint32_t tmem, float inv_sqrt_d) {
+__device__ void math_item(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
+                          void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
+                          int kt, int nkt, int n_tiles, uint32_t g0, uint32_t tmem, float inv_sqrt_d, bool& ok) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rq = warp & 3;                 // TMEM lane quarter
@@ -902,7 +1014,6 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   const int chunk0 = 4 * (qk & 1);         // first 16-byte chunk of this quarter in a 128-byte row
   float gsum = 0.f;
   float2 gsum2 = splat2(0.f);   // packed partial of gsum from interior key groups
-  bool ok = true;
 
   // row statistics of the next query tile are loaded one iteration ahead
   float nm = 0.f, nz = 1.f, nd = 0.f;
@@ -923,7 +1034,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
       nz = stats[2 * ri + 1];
       nd = rowdot[ri];
     }
-    const bool got = mbar_wait(&sm.bar_s_full, t & 1, ab);
+    const bool got = mbar_wait(&sm.bar_s_full, (g0 + t) & 1, ab);
     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
     tc_fence_after();
     const float m2 = row_ok ? fmaf(m, kLog2e, lg2_approx(zrow)) : 0.f;   // E = e^{s-m} / Z
@@ -972,7 +1083,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     // which still read the shared P/dS buffer; their latency hides behind this work
     CA_KEYS8_ANY(0, s16, p16, kbase);
     if (t > 0) {
-      const bool got2 = mbar_wait(&sm.bar_mma_done, (t - 1) & 1, ab);
+      const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
       if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
     }
     store_chunk(prow, drow, chunk0, swz, pk, dk);
@@ -996,10 +1107,10 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     // dQ of the previous query tile: TMEM -> swizzled f32 staging tile, which the
     // producer adds into the global accumulator with two TMA reduces once every
     // warp has arrived on p_ready.  The staging tile is free once the reduce of
-    // tile t-2 has read it.
+    // global tile g0+t-2 has read it.
     if (t > 0) {
-      if (t > 1) {
-        const bool got3 = mbar_wait(&sm.bar_dq_free, t & 1, ab);
+      if (g0 + t > 1) {
+        const bool got3 = mbar_wait(&sm.bar_dq_free, (g0 + t) & 1, ab);
         if (!__all_sync(0xffffffffu, got3)) { ok = false; break; }
       }
       uint32_t qv[16];
@@ -1013,11 +1124,11 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   }
 
   // last dQ tile (staged for the producer's final reduce) and the dK / dV accumulators
-  if (ok) ok = mbar_wait(&sm.bar_mma_done, (n_tiles - 1) & 1, ab);
+  if (ok) ok = mbar_wait(&sm.bar_mma_done, (g0 + n_tiles - 1) & 1, ab);
   ok = __all_sync(0xffffffffu, ok);
   tc_fence_after();
   if (ok) {
-    if (n_tiles > 1) ok = mbar_wait(&sm.bar_dq_free, n_tiles & 1, ab);
+    if (g0 + n_tiles > 1) ok = mbar_wait(&sm.bar_dq_free, (g0 + n_tiles) & 1, ab);
     ok = __all_sync(0xffffffffu, ok);
     uint32_t qv[16];
     tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
@@ -1063,6 +1174,36 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   }
 }
 
+// The math warps' item loop.  At each item boundary thread 0 alone waits for the
+// producer's published item (or gives up on an abort) and every math warp then
+// takes its decision, so all of them run the same items and the same named
+// barriers.
+template <bool kBF16>
+__device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
+                           void* dkp, void* dvp, float* gain_part, int BH, int H, int Tn, int nkt, int n_items,
+                           uint32_t tmem, float inv_sqrt_d) {
+  volatile int* ab = &sm.abort_flag;
+  uint32_t g0 = 0;
+  uint32_t published = 0;
+  bool ok = true;
+  while (true) {
+    named_bar_sync(2, NUM_MATH_WARPS * 32);
+    if (threadIdx.x == 0) {
+      const bool got = ok && mbar_wait(&sm.bar_item, published & 1, ab);
+      sm.decision = got ? sm.item : n_items;
+    }
+    ++published;
+    named_bar_sync(2, NUM_MATH_WARPS * 32);
+    const int item = sm.decision;
+    if (item >= n_items) break;
+    const Item it = decode_item(item, BH, nkt);
+    math_item<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, it.bh, it.bh % H, Tn, it.j0, it.kt, nkt,
+                     it.n, g0, tmem, inv_sqrt_d, ok);
+    ok = ok && !*ab;
+    g0 += it.n;
+  }
+}
+
 template <bool kBF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -1070,15 +1211,13 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ log_gain,
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            void* __restrict__ dkp, void* __restrict__ dvp,
-           float* __restrict__ gain_part, int BH, int H, int Tn, float inv_sqrt_d) {
+           float* __restrict__ gain_part, unsigned* __restrict__ counter, int BH, int H, int Tn,
+           float inv_sqrt_d) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = (Tn + BN - 1) / BN;
-  const int bh = blockIdx.x % BH;
-  const int kt = blockIdx.x / BH;           // low key tiles see the most query tiles: launch first
-  const int j0 = kt * BN;
-  const int n_tiles = nkt - kt;             // query tiles j0, j0+128, ...
+  const int n_items = BH * nkt;             // (bh, key tile) pairs, heaviest (kt = 0) first
 
   if (warp == NUM_MATH_WARPS) {
     if (lane == 0) {
@@ -1090,6 +1229,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       mbar_init(&sm.bar_mma_done, 1);
       mbar_init(&sm.bar_drain, 1);
       mbar_init(&sm.bar_dq_free, 1);
+      mbar_init(&sm.bar_item, 1);
       sm.abort_flag = 0;
       fence_mbar_init();
       tma_prefetch_desc(&tm_q);
@@ -1112,11 +1252,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   pdl_launch_dependents();
 
   if (warp == NUM_MATH_WARPS) {
-    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, bh, j0, n_tiles, tmem);   // whole warp, converged
+    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, tmem);   // converged
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, bh, bh % H, Tn, j0, kt, nkt,
-                      n_tiles, tmem, inv_sqrt_d);
+    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, n_items, tmem,
+                      inv_sqrt_d);
   }
   tc_fence_before();
   __syncthreads();
@@ -1178,6 +1318,19 @@ static bool make_map_f32(CUtensorMap* m, void* base, long long BH, long long T) 
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// SM count of the calling thread's current device (cached per device)
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 bool forward_supported(const FwdArgs& a) {
   return (a.dtype == 1 || a.dtype == 2) && a.D == 64 && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
          aligned16(a.o) && (!a.o_f32 || aligned16(a.o_f32)) && encode_fn() != nullptr;
@@ -1214,15 +1367,19 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
       !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH) ||
       !make_map_f32(&mdq, w.dq_acc, BH, a.T))
     return cudaErrorInvalidValue;
-  cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc);
+  cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc, w.counter);
   if (e != cudaSuccess) return e;
   auto kern = bwd::bwd_kernel<kBF16>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;
-  e = launch_pdl(kern, dim3((unsigned)(BH * nkt)), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo,
-                 mdq, a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv,
-                 a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
+  const long long n_items = BH * nkt;
+  // persistent: one CTA per SM (at most one per work item); items beyond the first
+  // gridDim.x come from the counter, which the prep kernel has zeroed
+  const unsigned grid = (unsigned)std::min<long long>(n_items, num_sms());
+  e = launch_pdl(kern, dim3(grid), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo, mdq,
+                 a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv, a.dlog_gain ? w.gain_part : nullptr,
+                 w.counter, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
   if (e != cudaSuccess) return e;
   return simt::launch_cast_dq(a, w.dq_acc, w.gain_part, (int)nkt);
 }
