@@ -662,8 +662,11 @@ __device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
 // dQ reduces advance once per tile, p_ready once per tile plus once per item (the
 // last dQ is staged after the item's tile loop), the Q/dO ring by stage.  The next
 // item's first Q/dO tiles go into the ring as soon as this item's last tiles free
-// their stages, and its K/V once this item's last gradient MMAs complete, so its
-// start overlaps this item's epilogue.
+// their stages, its K'/V' boxes are prefetched into L2 when it is claimed and
+// copied in once this item's last gradient MMAs complete, it is published to the
+// math warps at this item's last tile, and this item's final dQ reduce waits until
+// the next item's first S/dP is issued: the next item's start overlaps this
+// item's epilogue.
 template <bool kBF16>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
                          const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int n_items,
@@ -733,29 +736,54 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     }
     return true;
   };
+  // the last dQ tile of an item is staged by the math warps after their tile loop
+  // (one more p_ready phase); its reduce is issued after the next item's first
+  // S/dP, so that the next item starts as early as its K'/V' allow
+  auto final_reduce = [&](const Item& pi) -> bool {
+    if (!mbar_wait_warp(&sm.bar_p_ready, pr & 1, ab)) return false;
+    ++pr;
+    tma_reduce_add_3d(tdq, sm.dqs[0], 0, pi.j0 + (pi.n - 1) * BM, pi.bh);
+    tma_reduce_add_3d(tdq, sm.dqs[1], 32, pi.j0 + (pi.n - 1) * BM, pi.bh);
+    bulk_commit_group();
+    bulk_wait_group_read0();
+    if (lane == 0) mbar_arrive(&sm.bar_dq_free);
+    __syncwarp();
+    return true;
+  };
   bool good = item < n_items;
   if (good) {
     const Item it = decode_item(item, BH, nkt);
     load_kv(it);
   }
   publish(good ? item : n_items);
+  bool pending = false;   // the previous item's last dQ tile still has to be reduced
+  Item prev = decode_item(0, BH, nkt);
   while (good) {
     const Item it = decode_item(item, BH, nkt);
     // The next item is claimed as late as its first Q/dO prefetch allows (the
     // item's second-to-last tile, or its start when it has one tile), so that the
     // counter hands the heaviest remaining items to the CTAs that free up first.
+    // Its K'/V' boxes are prefetched into L2 at once; the shared-memory copy
+    // follows when this item's last gradient MMAs have read K'.
     bool has_next = false;
     Item nx = decode_item(0, BH, nkt);
     auto claim = [&]() {
       next = fetch();
       has_next = next < n_items;
-      if (has_next) nx = decode_item(next, BH, nkt);
+      if (has_next) {
+        nx = decode_item(next, BH, nkt);
+        tma_prefetch_l2_3d(tk, 0, max(nx.j0 - KOFF, 0), nx.bh);
+        tma_prefetch_l2_3d(tv, 0, max(nx.j0 - KOFF, 0), nx.bh);
+      }
     };
     next = -1;
     if (it.n == 1) claim();
-    if (!ensure_loaded(it, has_next, nx, g0 + (uint32_t)min(QSTAGES, it.n))) break;
+    if (!ensure_loaded(it, has_next, nx, g0 + (uint32_t)min(QSTAGES, it.n))) { good = false; break; }
     const int st0 = (int)(g0 % QSTAGES);
-    if (!mbar_wait_warp(&sm.bar_kv, kv_phase, ab) || !mbar_wait_warp(&sm.bar_qdo[st0], q_phase[st0], ab)) break;
+    if (!mbar_wait_warp(&sm.bar_kv, kv_phase, ab) || !mbar_wait_warp(&sm.bar_qdo[st0], q_phase[st0], ab)) {
+      good = false;
+      break;
+    }
     kv_pending = false;
     kv_phase ^= 1;
     q_pending[st0] = false;
@@ -763,6 +791,10 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     tc_fence_after();
     issue_s_dp<kBF16>(sm, st0, tmem, id_s);
     mma_commit(&sm.bar_s_full);
+    if (pending) {
+      if (!final_reduce(prev)) { good = false; break; }
+      pending = false;
+    }
     for (int t = 0; t < it.n && good; ++t) {
       const uint32_t g = g0 + t;
       const int st = (int)(g % QSTAGES);
@@ -790,11 +822,15 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         tma_reduce_add_3d(tdq, sm.dqs[1], 32, it.j0 + (t - 1) * BM, it.bh);
         bulk_commit_group();
       }
+      // every math warp is inside this item (it arrived on this tile's p_ready), so
+      // the published slot is free: the next item goes out now, and the math warps
+      // find it when they finish this one
+      if (last) publish(has_next ? next : n_items);
       // stage st takes global tile g + QSTAGES (this item's or the next item's)
       if (!ensure_loaded(it, has_next, nx, g + QSTAGES + 1)) { good = false; break; }
       if (last && has_next) {
-        // K' and V' are read by S/dP and by this tile's dQ MMAs: the next item's
-        // go in once the latter have completed
+        // K' is read by this tile's dQ MMAs: the next item's K'/V' go in once those
+        // have completed
         if (completed < (int)g) {
           if (!mbar_wait_warp(&sm.bar_mma_done, g & 1, ab)) { good = false; break; }
           completed = (int)g;
@@ -806,24 +842,15 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         if (lane == 0) mbar_arrive(&sm.bar_dq_free);
         __syncwarp();
       }
-      if (last) {
-        // the item's last dQ tile is staged after its tile loop (one more p_ready phase)
-        if (!mbar_wait_warp(&sm.bar_p_ready, pr & 1, ab)) { good = false; break; }
-        ++pr;
-        tma_reduce_add_3d(tdq, sm.dqs[0], 0, it.j0 + t * BM, it.bh);
-        tma_reduce_add_3d(tdq, sm.dqs[1], 32, it.j0 + t * BM, it.bh);
-        bulk_commit_group();
-        bulk_wait_group_read0();
-        if (lane == 0) mbar_arrive(&sm.bar_dq_free);
-        __syncwarp();
-      }
     }
     if (!good) break;
+    pending = true;
+    prev = it;
     g0 += it.n;
     item = next;
     good = item < n_items;
-    publish(good ? item : n_items);
   }
+  if (pending && !*ab) final_reduce(prev);   // the loop ended normally: the last item's last dQ tile
   // drain: every copy lands and every MMA completes before shared memory / TMEM go away
   mma_commit(&sm.bar_drain);
   int dummy = 0;

@@ -110,6 +110,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3-D tiled prefetch of a box into L2 (no shared-memory destination, nothing to
+// wait for; a hint that later loads of the box hit L2).  Lane 0.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile(
+      "{\n\t" CA_LANE0_PRED "@l0 cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 // 3-D tiled reduce-add of a shared-memory box into global memory (element type of
 // the tensor map, here f32), tracked by the issuing thread's bulk async-groups.
 // Rows outside the tensor are skipped.  Lane 0 (as is bulk_commit_group; the
