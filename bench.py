@@ -31,6 +31,7 @@ workload and prints the same line with "impl": "reference".
 from __future__ import annotations
 
 import argparse
+import contextlib
 import datetime
 import json
 import math
@@ -82,6 +83,39 @@ def _profile_traffic(kernel_tag: str):
     return None
 
 
+def _pci_bus_id(local: int) -> str:
+    """PCI bus id of CUDA device `local` (nvidia-smi and NVML index GPUs their own way)."""
+    p = torch.cuda.get_device_properties(local)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+
+
+@contextlib.contextmanager
+def _gpu_local_cpus(local: int):
+    """Run the block on the host CPUs NVML reports as local to GPU `local`, so that
+    pinned host buffers allocated inside sit on that GPU's NUMA node; the previous
+    CPU affinity is restored afterwards.  Yields whether the binding took effect."""
+    old = os.sched_getaffinity(0)
+    bound = False
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(_pci_bus_id(local).encode())
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+            cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (int(m) >> b) & 1} & old
+            if cpus and cpus != old:
+                os.sched_setaffinity(0, cpus)
+                bound = True
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:
+        bound = False
+    try:
+        yield bound
+    finally:
+        os.sched_setaffinity(0, old)
+
+
 class ClockSampler:
     """Samples nvidia-smi SM clocks and throttle reasons while running."""
 
@@ -97,7 +131,8 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "-i", _pci_bus_id(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -363,9 +398,10 @@ def run_ours(args, world, rank, local):
     # overlap step i-1's compute, and its device->host copies (s_out) overlap step
     # i+1's; input and host-output buffers are double-buffered.  Every step still
     # moves its own inputs in and its own gradients out inside the timed region.
-    host = [tuple(t.cpu().pin_memory() for t in sets[j]) for j in range(2)]
-    outs = [[torch.empty(SHAPE, dtype=dtype).pin_memory() for _ in range(3)] +
-            [torch.empty(H, dtype=torch.float32).pin_memory()] for _ in range(2)]
+    with _gpu_local_cpus(local) as numa_bound:
+        host = [tuple(t.cpu().pin_memory() for t in sets[j]) for j in range(2)]
+        outs = [[torch.empty(SHAPE, dtype=dtype).pin_memory() for _ in range(3)] +
+                [torch.empty(H, dtype=torch.float32).pin_memory()] for _ in range(2)]
     dev_in = [[torch.empty(SHAPE, dtype=dtype, device=dev) for _ in range(4)] for _ in range(2)]
     lg_req = torch.zeros(H, device=dev, requires_grad=True)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -465,6 +501,7 @@ def run_ours(args, world, rank, local):
                        "l2": f"{N_INPUT_SETS} rotating input sets (~{N_INPUT_SETS * 92} MB) > 126 MB L2",
                        "vs_baseline_ref": "reference CUDA v6, 1x V100 fp16, 16.603 ms (README.md:97)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "host_buffers_numa_local": numa_bound,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
             "roofline": roofline,
             "cpu_baseline": cpu,
