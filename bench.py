@@ -22,7 +22,9 @@ config 4, 101,205,120 parameters, 8 x 2048 random bytes per GPU, bf16 autocast,
 AdamW) in tokens/s over all ranks, with DDP over NCCL when N > 1
 (``--no-decoder`` skips it), and at N=1 "tinylm": the reference's 5M-parameter
 TinyLM in its fixed-tau CA variant P (fp32, batch 8, T = 192 and 512), the
-training step run as one CUDA graph (``--no-tinylm`` skips it).
+training step run as one CUDA graph (``--no-tinylm`` skips it), and "config3_sharded":
+BASELINE config 3 at B = 8, [8,16,16384,64], its 128 head-sequences split over the
+ranks (strong scaling, ``--no-config3`` skips it).
 
 ``--impl reference`` times the reference algorithm's CPU path (the float32
 restatement in oracle/, all host threads) on a bounded sample of the same
@@ -297,6 +299,52 @@ def run_decoder(args, world, rank, local, steps: int, warmup: int):
             "final_loss": float(loss.item()) if loss is not None else None, "data": "synthetic uniform bytes"}
 
 
+def run_config3_sharded(world, rank, local, T: int = 16384, steps: int = 5, warmup: int = 2):
+    """BASELINE config 3 across the ranks: [8,16,T,64] bf16 with q, k ~ N(0, 2^2) (score
+    std about 4) and a seeded 10% of keys duplicating their left neighbour, fwd+bwd
+    through the public op.  The 128 head-sequences are split into contiguous slices,
+    one per rank, with no communication: the total work is fixed, so this is the
+    operator's strong scaling.  Returns a dict for the JSON line."""
+    import continuum_attention_b200 as ca
+    from continuum_attention_b200.distributed import bh_shard
+    B, H, D = 8, 16, 64
+    start, end = bh_shard(B, H, world, rank)
+    n = end - start
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device="cpu").manual_seed(3000 + rank)
+    q = (torch.randn(1, n, T, D, generator=g) * 2).to(dev, torch.bfloat16)
+    k = torch.randn(1, n, T, D, generator=g) * 2
+    dup = torch.rand(T, generator=g) < 0.1
+    dup[0] = False
+    for j in torch.nonzero(dup).flatten().tolist():
+        k[:, :, j] = k[:, :, j - 1]
+    k = k.to(dev, torch.bfloat16)
+    v, dy = (torch.randn(1, n, T, D, generator=g).to(dev, torch.bfloat16) for _ in range(2))
+    lg = torch.zeros(n, device=dev, requires_grad=True)   # gain 1; one entry per head-sequence of the slice
+
+    def step():
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        y = ca.continuum_attention(qq, kk, vv, lg, 128)
+        return torch.autograd.grad(y, (qq, kk, vv, lg), dy)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(world, e0.elapsed_time(e1))
+    flops = 4.0 * B * H * T * T * D
+    return {"metric": f"CA fwd+bwd TFLOP/s, BASELINE config 3 at B=8 ([8,16,{T},64] bf16) over all ranks",
+            "value": flops * steps / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "head_sequences_per_rank": n, "scaling": "strong",
+            "parallelism": f"bh-shard x{world}", "data": "synthetic (score std 4, 10% duplicated keys)"}
+
+
 def run_tinylm(local, steps: int = 50):
     """TinyLM P (fixed tau 0.30, fp32 as the reference trains it) training tokens/s on
     one GPU at the reference's defaults (batch 8, T = 192) and at T = 512: the
@@ -488,6 +536,7 @@ def run_ours(args, world, rank, local):
     if not args.no_decoder:
         decoder = run_decoder(args, world, rank, local, steps=args.decoder_steps, warmup=3)
     tinylm = run_tinylm(local) if (world == 1 and not args.no_tinylm) else None
+    config3 = None if args.no_config3 else run_config3_sharded(world, rank, local)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -509,6 +558,7 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "decoder": decoder,
             "tinylm": tinylm,
+            "config3_sharded": config3,
         }
         print(json.dumps(line), flush=True)
 
@@ -524,6 +574,7 @@ def main():
     p.add_argument("--no-decoder", action="store_true", help="skip the CA-S decoder tokens/s measurement")
     p.add_argument("--decoder-steps", type=int, default=10)
     p.add_argument("--no-tinylm", action="store_true", help="skip the TinyLM-P small-model measurement")
+    p.add_argument("--no-config3", action="store_true", help="skip the config-3 strong-scaling measurement")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
