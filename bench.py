@@ -532,6 +532,15 @@ def run_ours(args, world, rank, local):
         cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
     clocks = clk.summary()
+    # The binding resource of both kernels is the special-function (MUFU) pipe and the
+    # scalar issue around it, not the tensor core: >= 2 MUFU ops (exp2, reciprocal) per
+    # causal score element per direction, 16 per clock per SM (nominal) at the sampled clock.
+    sm_hz = (clocks["sm_mhz"] if clocks else 1965.0) * 1e6
+    mufu_ops = 4.0 * n_elem
+    mufu_peak = 16.0 * torch.cuda.get_device_properties(local).multi_processor_count * sm_hz
+    roofline_mufu = {"bound": "mufu", "ops_per_step": mufu_ops, "achieved": mufu_ops / (ms_step * 1e-3),
+                     "peak": mufu_peak, "unit": "ops/s", "frac": mufu_ops / (ms_step * 1e-3) / mufu_peak,
+                     "peak_source": "nominal 16 MUFU ops/clock/SM x SMs x sampled SM clock; whole step"}
     decoder = None
     if not args.no_decoder:
         decoder = run_decoder(args, world, rank, local, steps=args.decoder_steps, warmup=3)
@@ -553,6 +562,7 @@ def run_ours(args, world, rank, local):
                     "host_buffers_numa_local": numa_bound,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
             "roofline": roofline,
+            "roofline_mufu": roofline_mufu,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": launches,

@@ -537,8 +537,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 }  // namespace fwd
 
 // ---------------------------------------------------------------------------
-// Backward, one CTA per 128-key tile [j0, j0+128), looping over the query
-// tiles i0 = j0, j0+128, ... (one CTA per SM):
+// Backward, persistent (one CTA per SM): a work item is one 128-key tile
+// [j0, j0+128) of one head-sequence, looping over the query tiles i0 = j0,
+// j0+128, ...; a CTA takes items heaviest first from a counter (see producer):
 //   warp 16 is the producer (the whole warp runs converged; lane 0 issues):
 //     TMA: K' and V' (keys j0-16 .. j0+143, stationary), Q and dO tiles (2 stages)
 //     S  = Q K'^T   128x160 fp32, TMEM columns [0,160)    (key j0+x at column 16+x)

@@ -99,3 +99,19 @@ def test_simt_and_auto_agree_bf16():
     assert norm_max_err(b[1], a[1]) < 1e-4
     for x, y in zip(b[2:], a[2:]):
         assert cosine(x, y) > 0.9999
+
+
+@pytest.mark.parametrize("shape", [(3, 37, 384, 64), (5, 60, 256, 64), (1, 1, 129, 64), (2, 80, 640, 64)])
+def test_persistent_backward_schedules_agree_with_simt(shape):
+    # Work-item counts from far below to far above the SM count (333, 600, 2 and 800 items
+    # of one to five query tiles): every item of the persistent tcgen05 backward must
+    # agree with the CUDA-core path, which schedules one block per tile.
+    B, H, T, D = shape
+    q, k, v, dy = gen_inputs(shape, 91 + T)
+    g = torch.Generator().manual_seed(T)
+    lg = torch.randn(H, generator=g) * 0.3
+    a, _ = run_op(q, k, v, lg, dy, dtype=torch.bfloat16, impl="simt")
+    b, _ = run_op(q, k, v, lg, dy, dtype=torch.bfloat16, impl="tcgen05")
+    assert norm_max_err(b[1], a[1]) < 1e-4
+    for name, x, y in zip(("dq", "dk", "dv", "dlog_gain"), b[2:], a[2:]):
+        assert cosine(x, y) > 0.9999, name
