@@ -348,6 +348,8 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     tmem_ld32(tS, sr[0]);
     tmem_ld32(tS + 32, sr[1]);
     tmem_ld_wait();
+    tmem_reg_fence(sr[0]);
+    tmem_reg_fence(sr[1]);
 #pragma unroll
     for (int c2 = 0; c2 < 2; ++c2) {
       if (diag) {
@@ -381,6 +383,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
       for (int half = 0; half < 2; ++half) {
         tmem_ld32(tO + 32 * half, sr[1]);
         tmem_ld_wait();
+        tmem_reg_fence(sr[1]);
 #pragma unroll
         for (int x = 0; x < 32; ++x) sr[1][x] = __float_as_uint(__uint_as_float(sr[1][x]) * alpha);
         tmem_st32(tO + 32 * half, sr[1]);
@@ -396,6 +399,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     uint32_t bufA[16], bufB[16];
     tmem_ld16(tS, bufA);
     tmem_ld_wait();
+    tmem_reg_fence(bufA);
 #define CA_FWD_CHUNK(BUF, CH)                                                                    \
   {                                                                                              \
     const int kind = fwd_chunk_kind(CH, kb, q0, warp, diag);                                     \
@@ -408,9 +412,11 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
       tmem_ld16(tS + 16 * (ch + 1), bufB);
       CA_FWD_CHUNK(bufA, ch);
       tmem_ld_wait();
+      tmem_reg_fence(bufB);
       if (ch + 2 < HB / 16) tmem_ld16(tS + 16 * (ch + 2), bufA);
       CA_FWD_CHUNK(bufB, ch + 1);
       tmem_ld_wait();
+      tmem_reg_fence(bufA);
     }
 #undef CA_FWD_CHUNK
     if (hh == nh - 1 && i == kb + HB - 1) {   // key i is the last key: its cap stays pending
@@ -430,6 +436,8 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   tmem_ld32(tO, oa[0]);
   tmem_ld32(tO + 32, oa[1]);
   tmem_ld_wait();
+  tmem_reg_fence(oa[0]);
+  tmem_reg_fence(oa[1]);
   if (!ok || !row_ok) return;
   float acc[HD];
 #pragma unroll
@@ -1080,6 +1088,12 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     tmem_ld16(colP, pv);
     tmem_ld1(colP + 16, p16);
     tmem_ld_wait();
+    tmem_reg_fence(s_lo);
+    tmem_reg_fence(sv);
+    tmem_reg_fence(s16);
+    tmem_reg_fence(p_lo);
+    tmem_reg_fence(pv);
+    tmem_reg_fence(p16);
     // the segment from the left halo key into key kbase
     float sa = __uint_as_float(s_lo) * scale;
     float ga = fmaf(__uint_as_float(p_lo), scale, -dds);
@@ -1124,6 +1138,10 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     tmem_ld16(colP + 16, pv);
     tmem_ld1(colP + 32, p_hi);
     tmem_ld_wait();
+    tmem_reg_fence(sv);
+    tmem_reg_fence(s_hi);
+    tmem_reg_fence(pv);
+    tmem_reg_fence(p_hi);
     tc_fence_before();
     mbar_arrive(&sm.bar_s_consumed);
     CA_KEYS8_ANY(0, s_hi, p_hi, kbase + 16);
@@ -1144,6 +1162,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
       uint32_t qv[16];
       tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
       tmem_ld_wait();
+      tmem_reg_fence(qv);
       stage_dq(sm, r, qk, qv);
     }
     fence_proxy_async_smem();
@@ -1161,6 +1180,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     uint32_t qv[16];
     tmem_ld16(tmem + lane_base + T_DQ + 16 * qk, qv);
     tmem_ld_wait();
+    tmem_reg_fence(qv);
     if (ok) {
       stage_dq(sm, r, qk, qv);
       fence_proxy_async_smem();
@@ -1174,6 +1194,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     uint32_t av[32];
     tmem_ld32(tmem + lane_base + (is_k ? T_DK : T_DV) + c0, av);
     tmem_ld_wait();
+    tmem_reg_fence(av);
     const int key = j0 + r;
     if (ok && key < Tn) {
       uint16_t* base = reinterpret_cast<uint16_t*>(is_k ? dkp : dvp) + ((size_t)bh * Tn + key) * HD + c0;

@@ -162,6 +162,18 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.ld writes its destination registers asynchronously: they hold the data
+// only after tcgen05.wait::ld.  The compiler sees the load's outputs as ready at
+// the load itself, so after the wait every loaded register goes through an empty
+// volatile asm that claims to rewrite it; uses of the register then depend on that
+// asm, which stays after the wait (volatile asm statements keep their order).
+__device__ __forceinline__ void tmem_reg_fence(uint32_t& r) { asm volatile("" : "+r"(r)); }
+template <int N>
+__device__ __forceinline__ void tmem_reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp receives lane
