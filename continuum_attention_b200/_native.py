@@ -35,6 +35,9 @@ SIGNATURES = {
     "ca_rope_qkv_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
     "ca_rope_qkv_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp]),
     "ca_selftest_wait_timeout": (_int, [_i64, _vp]),
+    "ca_rmsnorm_workspace_size": (_sz, [_i64, _i64]),
+    "ca_rmsnorm_forward": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _int, _vp]),
+    "ca_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _int, _vp]),
 }
 
 _lock = threading.Lock()

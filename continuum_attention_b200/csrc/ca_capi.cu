@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <initializer_list>
 #include <string>
 
 #include "ca_internal.h"
@@ -208,6 +209,71 @@ int ca_rope_qkv_backward(const void* dq, const void* dk, const void* dv, const f
   cudaError_t e = ca::rope::backward(dq, dk, dv, cos_sin, dqkv, B, T, H, D, dtype, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "ca_rope_qkv_backward launch");
   g_last_launches = 1;
+  return ok();
+}
+
+static int check_norm(const char* fn, int64_t rows, int64_t D, int x_dtype, int y_dtype) {
+  if (rows < 0 || D < 0)
+    return fail(CA_ERR_INVALID_ARGUMENT, "%s: negative shape [rows,D]=[%lld,%lld]", fn, (long long)rows,
+                (long long)D);
+  if ((x_dtype != CA_DTYPE_F32 && x_dtype != CA_DTYPE_BF16) || (y_dtype != CA_DTYPE_F32 && y_dtype != CA_DTYPE_BF16))
+    return fail(CA_ERR_UNSUPPORTED, "%s: dtypes must be float32 or bfloat16 (codes %d, %d)", fn, x_dtype, y_dtype);
+  if (!ca::norm::supported_dim(D))
+    return fail(CA_ERR_UNSUPPORTED, "%s: D=%lld must be 128, 256, 512 or 1024", fn, (long long)D);
+  return CA_OK;
+}
+
+static bool all_aligned16(std::initializer_list<const void*> ps) {
+  uintptr_t m = 0;
+  for (const void* p : ps) m |= (uintptr_t)p;
+  return (m & 15) == 0;
+}
+
+size_t ca_rmsnorm_workspace_size(int64_t rows, int64_t D) {
+  if (rows <= 0 || D <= 0) return 0;
+  return align_up(ca::norm::workspace_floats(rows, D) * sizeof(float));
+}
+
+int ca_rmsnorm_forward(const void* x, const float* w, void* y, float* rstd, int64_t rows, int64_t D, float eps,
+                       int x_dtype, int y_dtype, void* stream) {
+  int st = check_norm("ca_rmsnorm_forward", rows, D, x_dtype, y_dtype);
+  if (st != CA_OK) return st;
+  if (!(eps >= 0.f)) return fail(CA_ERR_INVALID_ARGUMENT, "ca_rmsnorm_forward: eps must be >= 0");
+  g_last_launches = 0;
+  if (rows == 0) return ok();
+  if (!x || !w || !y || !rstd) return fail(CA_ERR_INVALID_ARGUMENT, "ca_rmsnorm_forward: null pointer");
+  if (!all_aligned16({x, w, y, rstd}))
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_rmsnorm_forward: buffers must be 16-byte aligned");
+  cudaError_t e = ca::norm::forward(x, w, y, rstd, rows, D, eps, x_dtype, y_dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_rmsnorm_forward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
+int ca_rmsnorm_backward(const void* x, const float* w, const void* dy, const float* rstd, void* dx, float* dw,
+                        void* workspace, size_t workspace_bytes, int64_t rows, int64_t D, int x_dtype, int y_dtype,
+                        void* stream) {
+  int st = check_norm("ca_rmsnorm_backward", rows, D, x_dtype, y_dtype);
+  if (st != CA_OK) return st;
+  g_last_launches = 0;
+  if (rows == 0) {
+    if (dw && D > 0) {
+      cudaError_t e = cudaMemsetAsync(dw, 0, (size_t)D * sizeof(float), (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "ca_rmsnorm_backward memset");
+    }
+    return ok();
+  }
+  if (!x || !w || !dy || !rstd || !dx || !dw || !workspace)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_rmsnorm_backward: null pointer");
+  if (!all_aligned16({x, w, dy, rstd, dx, dw, workspace}))
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_rmsnorm_backward: buffers must be 16-byte aligned");
+  const size_t need = ca_rmsnorm_workspace_size(rows, D);
+  if (workspace_bytes < need)
+    return fail(CA_ERR_WORKSPACE, "ca_rmsnorm_backward: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  cudaError_t e = ca::norm::backward(x, w, dy, rstd, dx, dw, (float*)workspace, rows, D, x_dtype, y_dtype,
+                                     (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_rmsnorm_backward launch");
+  g_last_launches = 2;
   return ok();
 }
 

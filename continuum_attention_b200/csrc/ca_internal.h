@@ -92,7 +92,19 @@ cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
 cudaError_t launch_wait_timeout_selftest(unsigned long long limit_ns, cudaStream_t s);
 }  // namespace sm100
 
-// device status word (bounded waits record CA_ERR_DEVICE_TIMEOUT here)
+// SM count of the calling thread's current device (cached per device)
+inline int num_sms_cached() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 namespace rope {
 // qkv [B][T][3][H][D] -> q, k (rotary embedding applied), v [B][H][T][D]; cos_sin float32 [T][D/2][2]
 cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, long long B, long long T,
@@ -101,6 +113,18 @@ cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, voi
 cudaError_t backward(const void* dq, const void* dk, const void* dv, const float* cos_sin, void* dqkv,
                      long long B, long long T, long long H, long long D, int dtype, cudaStream_t s);
 }  // namespace rope
+
+namespace norm {
+// RMSNorm over the last axis (D in {128, 256, 512, 1024}); dtype codes as the ABI's
+// (0 f32, 1 bf16): x in x_dtype, y / dy in y_dtype, w / dw / rstd float32.
+bool supported_dim(long long D);
+cudaError_t forward(const void* x, const float* w, void* y, float* rstd, long long rows, long long D, float eps,
+                    int x_dtype, int y_dtype, cudaStream_t s);
+cudaError_t backward(const void* x, const float* w, const void* dy, const float* rstd, void* dx, float* dw,
+                     float* dw_part, long long rows, long long D, int x_dtype, int y_dtype, cudaStream_t s);
+// floats of scratch backward needs (per-block partials of dw)
+size_t workspace_floats(long long rows, long long D);
+}  // namespace norm
 
 cudaError_t read_device_status(int* out, bool reset);
 

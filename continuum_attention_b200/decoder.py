@@ -11,7 +11,7 @@ initialised with std 0.02/sqrt(2 n_layers)).
 ``attention_fn`` defaults to the CUDA operator; tests on machines without a GPU
 pass a CPU stand-in with the same signature.  On CUDA the attention block's
 input side is one native kernel (``rope.rope_qkv``: QKV unpacking fused with the
-rotary embedding) and the norms are fused ``F.rms_norm`` kernels.
+rotary embedding) and each norm is one native kernel forward (``rmsnorm``).
 """
 from __future__ import annotations
 
@@ -24,6 +24,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import continuum_attention
+from .rmsnorm import rms_norm as native_rms_norm
+from .rmsnorm import supported as native_rms_norm_supported
 from .rope import apply_rope_torch, rope_qkv
 
 
@@ -54,7 +56,13 @@ class ContinuumDecoderConfig:
 
 
 class RMSNorm(nn.Module):
-    """weight * x * rsqrt(mean(x^2) + eps) (cuda/continuum_attention.py:815-821), one fused kernel."""
+    """weight * x * rsqrt(mean(x^2) + eps) (cuda/continuum_attention.py:815-821).
+
+    On CUDA with a model width the native kernels cover (128, 256, 512, 1024;
+    float32 or bfloat16) it runs ``rmsnorm.rms_norm``, writing its output in the
+    autocast dtype the following projection consumes; elsewhere (CPU tests, other
+    widths) torch's fused ``F.rms_norm``.
+    """
 
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
@@ -62,6 +70,11 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
+        out_dtype = x.dtype
+        if x.is_cuda and torch.is_autocast_enabled("cuda"):
+            out_dtype = torch.get_autocast_dtype("cuda")
+        if native_rms_norm_supported(x, out_dtype):
+            return native_rms_norm(x, self.weight, self.eps, out_dtype)
         return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 

@@ -157,9 +157,28 @@ int ca_rope_qkv_forward(const void* qkv, const float* cos_sin, void* q, void* k,
 int ca_rope_qkv_backward(const void* dq, const void* dk, const void* dv, const float* cos_sin, void* dqkv,
                          int64_t B, int64_t T, int64_t H, int64_t D, int dtype, void* stream);
 
+/*
+ * CA-S decoder block RMSNorm (cuda/continuum_attention.py:815-821, the module
+ * RMSNorm: y = w * x * rsqrt(mean(x^2) + eps) over the last axis).  No
+ * reference counterpart in native code: the reference runs it as separate torch
+ * kernels.  x [rows][D] in x_dtype, y [rows][D] in y_dtype (float32 or
+ * bfloat16 each: the block writes the bfloat16 input of the next projection
+ * directly), w float32 [D], rstd float32 [rows] (written by the forward, read by
+ * the backward).  D in {128, 256, 512, 1024}; buffers 16-byte aligned.
+ * The backward writes dx [rows][D] (x_dtype) and dw float32 [D] (summed over
+ * rows in a fixed order) and needs ca_rmsnorm_workspace_size() bytes of
+ * scratch.  One launch forward, two backward, no allocation.
+ */
+size_t ca_rmsnorm_workspace_size(int64_t rows, int64_t D);
+int ca_rmsnorm_forward(const void* x, const float* w, void* y, float* rstd, int64_t rows, int64_t D, float eps,
+                       int x_dtype, int y_dtype, void* stream);
+int ca_rmsnorm_backward(const void* x, const float* w, const void* dy, const float* rstd, void* dx, float* dw,
+                        void* workspace, size_t workspace_bytes, int64_t rows, int64_t D, int x_dtype, int y_dtype,
+                        void* stream);
+
 /* Number of kernels the last successful ca_forward / ca_backward /
- * ca_rope_qkv_* call on this thread enqueued (memsets excluded).  Diagnostic
- * for launch accounting. */
+ * ca_rope_qkv_* / ca_rmsnorm_* call on this thread enqueued (memsets
+ * excluded).  Diagnostic for launch accounting. */
 int ca_last_launch_count(void);
 
 /*

@@ -91,3 +91,14 @@ def test_python_wrapper_rejects_cpu_tensors_without_fallback():
         ca.continuum_attention(q, q, q, torch.zeros(2))
     with pytest.raises(ValueError, match="must share dtype"):
         ca.continuum_attention(q, q.double(), q, torch.zeros(2))
+
+
+def test_rmsnorm_argument_checks_on_cpu():
+    lib = _native.lib()
+    # rejected before any device work: unsupported width, unsupported dtype, null pointers
+    assert lib.ca_rmsnorm_forward(None, None, None, None, 4, 768, 1e-6, 0, 1, None) == 2
+    assert lib.ca_rmsnorm_forward(None, None, None, None, 4, 1024, 1e-6, 2, 1, None) == 2
+    assert lib.ca_rmsnorm_forward(None, None, None, None, 4, 1024, 1e-6, 0, 1, None) == 1
+    assert b"null" in lib.ca_last_error()
+    assert lib.ca_rmsnorm_forward(None, None, None, None, 0, 1024, 1e-6, 0, 1, None) == 0
+    assert lib.ca_rmsnorm_workspace_size(0, 1024) == 0
