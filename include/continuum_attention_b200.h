@@ -105,7 +105,9 @@ size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, in
  * (which may then be NULL), keeping bf16/f16 score gradients free of the
  * output rounding.
  * workspace must hold ca_backward_workspace_size() bytes (256-byte aligned);
- * its contents on entry are ignored.
+ * its contents on entry are ignored, and it belongs to this call until the
+ * call's GPU work has finished (calls whose work may overlap on the GPU need
+ * separate workspaces: the backward's work counter lives there too).
  * Replaces _CAExactTiled.backward, cuda/continuum_attention.py:696-766.
  */
 int ca_backward(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
