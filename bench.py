@@ -53,7 +53,7 @@ if ROOT not in sys.path:
 SHAPE = (2, 16, 2048, 64)
 METRIC = "CA fwd+bwd TFLOP/s @[2,16,2048,64] bf16 (4*B*H*T^2*D per step)"
 UNIT = "TFLOP/s"
-# reference CUDA v6 on one V100, fp16, same shape: 16.603 ms total
+# published reference figure: CUDA v6 on one V100, fp16, same shape, 16.603 ms per fwd+bwd (README.md:97 of the reference)
 PUBLISHED_V100_V6_MS = 16.603
 N_INPUT_SETS = 8   # rotating input sets, 8 x ~92 MB >> 126 MB L2
 
