@@ -150,25 +150,40 @@ __global__ void __launch_bounds__(WARPS * 32) bwd_kernel(const TX* __restrict__ 
   }
 }
 
-// dw[col] = sum of the blocks' partials.  A block takes 32 columns (lane = column);
-// warp k adds the partial rows k, k+8, ... in order, then warp 0 adds the eight
-// warp sums in order: a fixed summation order, so dw is reproducible.
-__global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ dw_part, float* __restrict__ dw,
-                                                        int nblocks, int D) {
+// dw[col] = sum of the blocks' partials.  A block of RW warps takes 32 columns
+// (lane = column); warp k adds the partial rows k, k+RW, k+2RW, ... into eight
+// accumulators (row k + RW(8i + a) into accumulator a, so eight independent loads
+// are in flight), folds them in order, and warp 0 adds the RW warp sums in order:
+// a fixed summation order, so dw is reproducible.
+constexpr int RW = 32;
+__global__ void __launch_bounds__(RW * 32) dw_reduce_kernel(const float* __restrict__ dw_part, float* __restrict__ dw,
+                                                            int nblocks, int D) {
   pdl_wait();
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
   float s = 0.f;
-  if (col < D)
-    for (int b = warp; b < nblocks; b += 8) s += dw_part[(size_t)b * D + col];
-  __shared__ float red[8][32];
+  if (col < D) {
+    float a[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) a[u] = 0.f;
+    int b = warp;
+    for (; b + 7 * RW < nblocks; b += 8 * RW) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] += dw_part[(size_t)(b + RW * u) * D + col];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (b + RW * u < nblocks) a[u] += dw_part[(size_t)(b + RW * u) * D + col];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += a[u];
+  }
+  __shared__ float red[RW][32];
   red[warp][lane] = s;
   __syncthreads();
   if (warp == 0 && col < D) {
     float t = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    for (int k = 0; k < RW; ++k) t += red[k][lane];
     dw[col] = t;
   }
 }
@@ -195,7 +210,7 @@ static cudaError_t bwd_t(const void* x, const float* w, const void* dy, const fl
                              (const TY*)dy, rstd, (TX*)dx, dw_part, rows);
   if (e != cudaSuccess) return e;
   constexpr int D = 128 * NC;
-  return launch_pdl(dw_reduce_kernel, dim3((D + 31) / 32), dim3(256), 0, s, (const float*)dw_part, dw, nb, D);
+  return launch_pdl(dw_reduce_kernel, dim3((D + 31) / 32), dim3(RW * 32), 0, s, (const float*)dw_part, dw, nb, D);
 }
 
 #define CA_NORM_DISPATCH(FN, ...)                                                          \

@@ -16,9 +16,10 @@
 // and its transpose for the gradient.  The caller passes the (c, s) table as
 // float32 [T][D/2][2]; arithmetic is fp32 with one rounding per output.
 //
-// Work unit: one thread per 8-element chunk of one (b, t, {q,k,v}, h) row; the
-// projection-side access is fully contiguous, the [B,H,T,D] side writes or
-// reads whole D-element rows.  HBM-bound: 2 x 3*B*T*H*D elements per pass.
+// Work unit: one block per token (b, t), one thread per 8-element chunk of its
+// [3][H][D] projection row; the projection-side access is fully contiguous, the
+// [B,H,T,D] side writes or reads whole D-element rows.  HBM-bound: 2 x 3*B*T*H*D
+// elements per pass.
 #include "ca_common.cuh"
 #include "ca_internal.h"
 
@@ -66,26 +67,24 @@ __device__ __forceinline__ void load8<__half>(const __half* p, float (&x)[8]) { 
 template <>
 __device__ __forceinline__ void store8<__half>(__half* p, const float (&x)[8]) { store8_16(p, x); }
 
+// One block per token (b, t); thread j of the token's 3*H*D/8 chunks takes
+// chunk c = j % (D/8) of head h = (j / (D/8)) % H of q, k or v (j / (H*D/8)):
+// 32-bit index arithmetic once per chunk instead of a 64-bit decomposition.
+
 // qkv [B][T][3][H][D] -> q, k (rotated), v [B][H][T][D]
 template <typename T>
 __global__ void pack_fwd_kernel(const T* __restrict__ qkv, const float2* __restrict__ cs, T* __restrict__ q,
-                                T* __restrict__ k, T* __restrict__ v, int Tn, int H, int D, size_t total) {
+                                T* __restrict__ k, T* __restrict__ v, int Tn, int H, int D) {
   pdl_wait();
   pdl_launch_dependents();
-  const int chunks = D / 8;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    size_t r = idx;
-    const int c = (int)(r % chunks);
-    r /= chunks;
-    const int h = (int)(r % H);
-    r /= H;
-    const int which = (int)(r % 3);
-    r /= 3;
-    const int t = (int)(r % Tn);
-    const size_t b = r / Tn;
+  const unsigned chunks = (unsigned)D / 8, per_head = chunks, per_which = (unsigned)H * chunks;
+  const unsigned token = blockIdx.x, t = token % (unsigned)Tn, b = token / (unsigned)Tn;
+  const T* src = qkv + (size_t)token * 3 * per_which * 8;
+  for (unsigned j = threadIdx.x; j < 3 * per_which; j += blockDim.x) {
+    const unsigned which = j / per_which, rem = j - which * per_which;
+    const unsigned h = rem / per_head, c = rem - h * per_head;
     float x[8];
-    load8<T>(qkv + idx * 8, x);
+    load8<T>(src + (size_t)j * 8, x);
     if (which < 2) {
       const float2* row = cs + (size_t)t * (D / 2) + 4 * c;
 #pragma unroll
@@ -97,32 +96,25 @@ __global__ void pack_fwd_kernel(const T* __restrict__ qkv, const float2* __restr
       }
     }
     T* dst = which == 0 ? q : (which == 1 ? k : v);
-    store8<T>(dst + ((b * H + h) * Tn + t) * D + 8 * c, x);
+    store8<T>(dst + (((size_t)b * H + h) * Tn + t) * D + 8 * c, x);
   }
 }
 
 // dq, dk, dv [B][H][T][D] -> dqkv [B][T][3][H][D] (transposed rotation on dq, dk)
 template <typename T>
 __global__ void pack_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv,
-                                const float2* __restrict__ cs, T* __restrict__ dqkv, int Tn, int H, int D,
-                                size_t total) {
+                                const float2* __restrict__ cs, T* __restrict__ dqkv, int Tn, int H, int D) {
   pdl_wait();
   pdl_launch_dependents();
-  const int chunks = D / 8;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    size_t r = idx;
-    const int c = (int)(r % chunks);
-    r /= chunks;
-    const int h = (int)(r % H);
-    r /= H;
-    const int which = (int)(r % 3);
-    r /= 3;
-    const int t = (int)(r % Tn);
-    const size_t b = r / Tn;
+  const unsigned chunks = (unsigned)D / 8, per_head = chunks, per_which = (unsigned)H * chunks;
+  const unsigned token = blockIdx.x, t = token % (unsigned)Tn, b = token / (unsigned)Tn;
+  T* dst = dqkv + (size_t)token * 3 * per_which * 8;
+  for (unsigned j = threadIdx.x; j < 3 * per_which; j += blockDim.x) {
+    const unsigned which = j / per_which, rem = j - which * per_which;
+    const unsigned h = rem / per_head, c = rem - h * per_head;
     const T* src = which == 0 ? dq : (which == 1 ? dk : dv);
     float x[8];
-    load8<T>(src + ((b * H + h) * Tn + t) * D + 8 * c, x);
+    load8<T>(src + (((size_t)b * H + h) * Tn + t) * D + 8 * c, x);
     if (which < 2) {
       const float2* row = cs + (size_t)t * (D / 2) + 4 * c;
 #pragma unroll
@@ -133,29 +125,29 @@ __global__ void pack_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ 
         x[2 * p + 1] = fmaf(o, w.x, -e * w.y);
       }
     }
-    store8<T>(dqkv + idx * 8, x);
+    store8<T>(dst + (size_t)j * 8, x);
   }
 }
 
-static unsigned grid_for(size_t total) {
-  const size_t blocks = (total + 255) / 256;
-  return (unsigned)(blocks < (size_t)148 * 32 ? blocks : (size_t)148 * 32);
+// threads per token block: the token's chunk count rounded up to whole warps, at most 1024
+static unsigned block_for(long long H, long long D) {
+  const long long n = 3 * H * (D / 8);
+  const long long w = (n + 31) / 32 * 32;
+  return (unsigned)(w < 1024 ? w : 1024);
 }
 
 template <typename T>
 static cudaError_t fwd_t(const void* qkv, const float* cs, void* q, void* k, void* v, long long B, long long Tn,
                          long long H, long long D, cudaStream_t s) {
-  const size_t total = (size_t)B * Tn * 3 * H * (D / 8);
-  return launch_pdl(pack_fwd_kernel<T>, dim3(grid_for(total)), dim3(256), 0, s, (const T*)qkv,
-                    (const float2*)cs, (T*)q, (T*)k, (T*)v, (int)Tn, (int)H, (int)D, total);
+  return launch_pdl(pack_fwd_kernel<T>, dim3((unsigned)(B * Tn)), dim3(block_for(H, D)), 0, s, (const T*)qkv,
+                    (const float2*)cs, (T*)q, (T*)k, (T*)v, (int)Tn, (int)H, (int)D);
 }
 
 template <typename T>
 static cudaError_t bwd_t(const void* dq, const void* dk, const void* dv, const float* cs, void* dqkv, long long B,
                          long long Tn, long long H, long long D, cudaStream_t s) {
-  const size_t total = (size_t)B * Tn * 3 * H * (D / 8);
-  return launch_pdl(pack_bwd_kernel<T>, dim3(grid_for(total)), dim3(256), 0, s, (const T*)dq, (const T*)dk,
-                    (const T*)dv, (const float2*)cs, (T*)dqkv, (int)Tn, (int)H, (int)D, total);
+  return launch_pdl(pack_bwd_kernel<T>, dim3((unsigned)(B * Tn)), dim3(block_for(H, D)), 0, s, (const T*)dq,
+                    (const T*)dk, (const T*)dv, (const float2*)cs, (T*)dqkv, (int)Tn, (int)H, (int)D);
 }
 
 cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, long long B, long long T,

@@ -172,3 +172,44 @@ def count_parameters(model: nn.Module) -> dict:
     params = list(model.parameters())
     return {"total": sum(p.numel() for p in params),
             "trainable": sum(p.numel() for p in params if p.requires_grad)}
+
+
+def _main(argv=None):
+    """Training-step throughput of the CA-S decoder on one GPU, synthetic bytes:
+    ``python -m continuum_attention_b200.decoder [--steps K] [--warmup W]``.
+    Prints one JSON line (tokens/s, ms per step, last loss)."""
+    import argparse
+    import json
+
+    from .distributed import build_adamw, train_step
+    p = argparse.ArgumentParser(description=_main.__doc__)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--seq-len", type=int, default=2048)
+    args = p.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(1337)
+    model = ContinuumDecoderLM(ContinuumDecoderConfig(block_size=args.seq_len)).to(dev)
+    opt = build_adamw(model)
+    g = torch.Generator(device="cpu").manual_seed(2000)
+    batch = torch.randint(0, 256, (args.batch, args.seq_len), generator=g).to(dev)
+    for _ in range(args.warmup):
+        train_step(model, opt, batch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    loss = None
+    for _ in range(args.steps):
+        loss = train_step(model, opt, batch)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    print(json.dumps({"metric": "CA-S decoder train tokens/s", "value": args.batch * args.seq_len / (ms * 1e-3),
+                      "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "loss": None if loss is None else float(loss.item()),
+                      "params": count_parameters(model)["total"]}))
+
+
+if __name__ == "__main__":
+    _main()
