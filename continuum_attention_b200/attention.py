@@ -27,6 +27,9 @@ _DTYPE_CODE = {torch.float32: _native.CA_DTYPE_F32, torch.bfloat16: _native.CA_D
 _IMPL_CODE = {"auto": _native.CA_IMPL_AUTO, "simt": _native.CA_IMPL_SIMT,
               "tcgen05": _native.CA_IMPL_TCGEN05}
 
+# storage order of the output o and of its gradient (q, k, v and their gradients are [B,H,T,D])
+_LAYOUT_CODE = {"bhtd": _native.CA_LAYOUT_BHTD, "bthd": _native.CA_LAYOUT_BTHD}
+
 
 def ctypes_ptr(t: torch.Tensor):
     return t.data_ptr() if t.numel() > 0 else None
@@ -53,25 +56,27 @@ def _validate(q, k, v, log_gain):
         raise ValueError(f"log_gain must have shape [H]=[{H}], got {tuple(log_gain.shape)}")
 
 
-def forward_raw(q, k, v, log_gain_f32, impl="auto", want_f32=False, want_stats=True):
+def forward_raw(q, k, v, log_gain_f32, impl="auto", want_f32=False, want_stats=True, out_layout="bhtd"):
     """Run the native forward; returns (o, row_stats or None, o_f32 or None).
 
     q, k, v contiguous CUDA [B,H,T,D]; log_gain_f32 contiguous float32 [H] on the
     same device.  ``want_stats=False`` is the inference form (no backward follows,
-    the per-row statistics are not written).  Used by the autograd op, the tests
-    and the benchmark.
+    the per-row statistics are not written).  ``out_layout="bthd"`` returns o as a
+    contiguous [B,T,H,D] tensor (the attention output projection's input order);
+    o_f32 stays [B,H,T,D].  Used by the autograd op, the tests and the benchmark.
     """
     B, H, T, D = q.shape
     lib = _native.lib()
-    o = torch.empty_like(q)
+    o = torch.empty((B, T, H, D), dtype=q.dtype, device=q.device) if out_layout == "bthd" else torch.empty_like(q)
     stats = (torch.empty(B * H * T * lib.ca_row_stats_floats(), dtype=torch.float32, device=q.device)
              if want_stats else None)
     o32 = torch.empty(q.shape, dtype=torch.float32, device=q.device) if want_f32 else None
     with torch.cuda.device(q.device):
-        st = lib.ca_forward(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), ctypes_ptr(log_gain_f32),
-                            ctypes_ptr(o), None if o32 is None else ctypes_ptr(o32),
-                            None if stats is None else ctypes_ptr(stats),
-                            B, H, T, D, _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _stream(q.device))
+        st = lib.ca_forward_ex(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), ctypes_ptr(log_gain_f32),
+                               ctypes_ptr(o), None if o32 is None else ctypes_ptr(o32),
+                               None if stats is None else ctypes_ptr(stats),
+                               B, H, T, D, _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _LAYOUT_CODE[out_layout],
+                               _stream(q.device))
     _native.check("ca_forward", st)
     return o, stats, o32
 
@@ -81,11 +86,12 @@ def workspace_bytes(B, H, T, D, dtype) -> int:
 
 
 def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="auto", workspace=None,
-                 o_f32=None):
+                 o_f32=None, layout="bhtd"):
     """Run the native backward; returns (dq, dk, dv, dlog_gain float32 [H] or None).
 
     ``o_f32`` (optional) is the forward's fp32 accumulator; it makes the row
-    terms D_i = dO_i . O_i exact to fp32 for bf16/f16 inputs.
+    terms D_i = dO_i . O_i exact to fp32 for bf16/f16 inputs.  ``layout="bthd"``:
+    o and do are contiguous [B,T,H,D] tensors.
     """
     B, H, T, D = q.shape
     lib = _native.lib()
@@ -95,12 +101,12 @@ def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="aut
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
-        st = lib.ca_backward(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v), None if o is None else ctypes_ptr(o),
-                             None if o_f32 is None else ctypes_ptr(o_f32), ctypes_ptr(do),
-                             ctypes_ptr(log_gain_f32), ctypes_ptr(stats), ctypes_ptr(dq), ctypes_ptr(dk),
-                             ctypes_ptr(dv), None if dg is None else ctypes_ptr(dg),
-                             workspace.data_ptr(), workspace.numel(), B, H, T, D,
-                             _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _stream(q.device))
+        st = lib.ca_backward_ex(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v),
+                                None if o is None else ctypes_ptr(o), None if o_f32 is None else ctypes_ptr(o_f32),
+                                ctypes_ptr(do), ctypes_ptr(log_gain_f32), ctypes_ptr(stats), ctypes_ptr(dq),
+                                ctypes_ptr(dk), ctypes_ptr(dv), None if dg is None else ctypes_ptr(dg),
+                                workspace.data_ptr(), workspace.numel(), B, H, T, D,
+                                _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _LAYOUT_CODE[layout], _stream(q.device))
     _native.check("ca_backward", st)
     return dq, dk, dv, dg
 
@@ -115,20 +121,25 @@ class ContinuumAttentionFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, q, k, v, log_gain, query_tile):
+    def forward(ctx, q, k, v, log_gain, query_tile, out_layout="bhtd"):
         _validate(q, k, v, log_gain)
+        if out_layout not in _LAYOUT_CODE:
+            raise ValueError(f"out_layout must be one of {sorted(_LAYOUT_CODE)}")
         lg = log_gain.detach().to(device=q.device, dtype=torch.float32).contiguous()
         lowp = q.dtype != torch.float32
+        # with out_layout "bthd" o is stored [B,T,H,D]; the op returns its [B,H,T,D] view
+        view = (lambda t: t.transpose(1, 2)) if out_layout == "bthd" else (lambda t: t)
         if not any(ctx.needs_input_grad[:4]):
             # inference: no backward can follow, so no statistics or fp32 output are kept
-            o, _, _ = forward_raw(q, k, v, lg, impl=_current_impl(), want_stats=False)
-            return o
-        o, stats, o32 = forward_raw(q, k, v, lg, impl=_current_impl(), want_f32=lowp)
+            o, _, _ = forward_raw(q, k, v, lg, impl=_current_impl(), want_stats=False, out_layout=out_layout)
+            return view(o)
+        o, stats, o32 = forward_raw(q, k, v, lg, impl=_current_impl(), want_f32=lowp, out_layout=out_layout)
         ctx.save_for_backward(q, k, v, o32 if lowp else o, stats, lg)
         ctx.lowp = lowp
         ctx.gain_dtype = log_gain.dtype
         ctx.query_tile = int(query_tile)
-        return o
+        ctx.out_layout = out_layout
+        return view(o)
 
     @staticmethod
     def backward(ctx, grad_y):
@@ -136,11 +147,15 @@ class ContinuumAttentionFunction(torch.autograd.Function):
             raise RuntimeError("CA analytic kernels support first-order gradients only")
         q, k, v, o_saved, stats, lg = ctx.saved_tensors
         want_dgain = bool(ctx.needs_input_grad[3])
+        g = grad_y.to(q.dtype)
+        # "bthd": the gradient of the [B,H,T,D] view of a [B,T,H,D] output, handed to the
+        # kernels in that storage order (a copy only when it does not arrive that way)
+        g = (g.transpose(1, 2) if ctx.out_layout == "bthd" else g).contiguous()
         # with the fp32 accumulator saved, the dtype-rounded output is not needed
-        dq, dk, dv, dg = backward_raw(q, k, v, None if ctx.lowp else o_saved, grad_y.to(q.dtype).contiguous(),
-                                      lg, stats, want_dgain=want_dgain, impl=_current_impl(),
-                                      o_f32=o_saved if ctx.lowp else None)
-        return dq, dk, dv, (dg.to(ctx.gain_dtype) if dg is not None else None), None
+        dq, dk, dv, dg = backward_raw(q, k, v, None if ctx.lowp else o_saved, g, lg, stats,
+                                      want_dgain=want_dgain, impl=_current_impl(),
+                                      o_f32=o_saved if ctx.lowp else None, layout=ctx.out_layout)
+        return dq, dk, dv, (dg.to(ctx.gain_dtype) if dg is not None else None), None, None
 
 
 _impl_override = {"impl": "auto"}
@@ -168,16 +183,21 @@ class use_impl:
         return False
 
 
-def continuum_attention(q, k, v, log_gain, query_tile=64):
+def continuum_attention(q, k, v, log_gain, query_tile=64, *, out_layout="bhtd"):
     """Exact causal Continuum Attention on [B,H,T,D] tensors.
 
     Drop-in for ``continuum_attention`` (cuda/continuum_attention.py:768-783):
     scores ``exp(log_gain[h]) * q.k / sqrt(D)``, piecewise-linear key/value
     trajectories integrated exactly per segment, half-token caps on the first
     and last visible key, causal.  Returns [B,H,T,D] in the input dtype.
+
+    ``out_layout="bthd"`` (no reference counterpart) stores the result [B,T,H,D]
+    and returns its [B,H,T,D] view, so ``y.transpose(1, 2).reshape(B, T, H*D)``
+    -- the attention output projection's input -- is free, and its gradient
+    reaches the backward without a transposing copy.
     """
     return ContinuumAttentionFunction.apply(q.contiguous(), k.contiguous(), v.contiguous(), log_gain,
-                                            int(query_tile))
+                                            int(query_tile), out_layout)
 
 
 def continuum_attention_fixed_tau(q, k, v, tau: float = 0.30):
@@ -186,4 +206,4 @@ def continuum_attention_fixed_tau(q, k, v, tau: float = 0.30):
         raise ValueError("fixed_tau must be > 0")
     H = q.shape[1]
     lg = torch.full((H,), math.log(1.0 / tau), dtype=torch.float32, device=q.device)
-    return ContinuumAttentionFunction.apply(q.contiguous(), k.contiguous(), v.contiguous(), lg, 64)
+    return ContinuumAttentionFunction.apply(q.contiguous(), k.contiguous(), v.contiguous(), lg, 64, "bhtd")

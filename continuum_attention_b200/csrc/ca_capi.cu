@@ -90,16 +90,24 @@ int ca_row_stats_floats(void) { return 2; }
 
 int ca_last_launch_count(void) { return g_last_launches; }
 
-int ca_forward(const void* q, const void* k, const void* v, const float* log_gain, void* o,
-               float* o_f32, float* row_stats, int64_t B, int64_t H, int64_t T, int64_t D,
-               int dtype, int impl, void* stream) {
+static int check_layout(const char* fn, int layout) {
+  if (layout != CA_LAYOUT_BHTD && layout != CA_LAYOUT_BTHD)
+    return fail(CA_ERR_INVALID_ARGUMENT, "%s: unknown activation layout code %d", fn, layout);
+  return CA_OK;
+}
+
+static int forward_impl(const void* q, const void* k, const void* v, const float* log_gain, void* o,
+                        float* o_f32, float* row_stats, int64_t B, int64_t H, int64_t T, int64_t D,
+                        int dtype, int impl, void* stream, int layout) {
   int st = check_shape(B, H, T, D, dtype, impl);
+  if (st != CA_OK) return st;
+  st = check_layout("ca_forward", layout);
   if (st != CA_OK) return st;
   if (B * H * T == 0) return ok();
   if (!q || !k || !v || !log_gain || !o)
     return fail(CA_ERR_INVALID_ARGUMENT, "ca_forward: null q/k/v/log_gain/o pointer");
   ca::FwdArgs a{q, k, v, log_gain, o, o_f32, row_stats, B, H, T, D, dtype,
-                (float)(1.0 / std::sqrt((double)D)), (cudaStream_t)stream};
+                (float)(1.0 / std::sqrt((double)D)), (cudaStream_t)stream, layout};
   cudaError_t e;
   g_last_launches = 0;
   if (impl == CA_IMPL_SIMT) {
@@ -120,17 +128,31 @@ int ca_forward(const void* q, const void* k, const void* v, const float* log_gai
   return ok();
 }
 
+int ca_forward(const void* q, const void* k, const void* v, const float* log_gain, void* o,
+               float* o_f32, float* row_stats, int64_t B, int64_t H, int64_t T, int64_t D,
+               int dtype, int impl, void* stream) {
+  return forward_impl(q, k, v, log_gain, o, o_f32, row_stats, B, H, T, D, dtype, impl, stream, CA_LAYOUT_BHTD);
+}
+
+int ca_forward_ex(const void* q, const void* k, const void* v, const float* log_gain, void* o,
+                  float* o_f32, float* row_stats, int64_t B, int64_t H, int64_t T, int64_t D,
+                  int dtype, int impl, int layout, void* stream) {
+  return forward_impl(q, k, v, log_gain, o, o_f32, row_stats, B, H, T, D, dtype, impl, stream, layout);
+}
+
 size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, int dtype) {
   (void)dtype;
   if (B <= 0 || H <= 0 || T <= 0 || D <= 0) return 0;
   return workspace_layout(B, H, T, D).total;
 }
 
-int ca_backward(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
-                const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
-                float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
-                int64_t T, int64_t D, int dtype, int impl, void* stream) {
+static int backward_impl(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                         const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk,
+                         void* dv, float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B,
+                         int64_t H, int64_t T, int64_t D, int dtype, int impl, void* stream, int layout) {
   int st = check_shape(B, H, T, D, dtype, impl);
+  if (st != CA_OK) return st;
+  st = check_layout("ca_backward", layout);
   if (st != CA_OK) return st;
   cudaStream_t s = (cudaStream_t)stream;
   if (B * H * T == 0) {
@@ -152,7 +174,7 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
   ca::BwdWorkspace w{(float*)(ws + l.rowdot), (float*)(ws + l.dq_acc), (float*)(ws + l.gain_part),
                      l.nparts, (unsigned*)(ws + l.counter)};
   ca::BwdArgs a{q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
-                (float)(1.0 / std::sqrt((double)D)), s};
+                (float)(1.0 / std::sqrt((double)D)), s, layout};
   cudaError_t e;
   g_last_launches = 0;
   if (impl == CA_IMPL_SIMT) {
@@ -170,6 +192,22 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
   }
   if (e != cudaSuccess) return cuda_fail(e, "ca_backward launch");
   return ok();
+}
+
+int ca_backward(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
+                float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                int64_t T, int64_t D, int dtype, int impl, void* stream) {
+  return backward_impl(q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, workspace,
+                       workspace_bytes, B, H, T, D, dtype, impl, stream, CA_LAYOUT_BHTD);
+}
+
+int ca_backward_ex(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                   const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
+                   float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                   int64_t T, int64_t D, int dtype, int impl, int layout, void* stream) {
+  return backward_impl(q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, workspace,
+                       workspace_bytes, B, H, T, D, dtype, impl, stream, layout);
 }
 
 static int check_rope(const char* fn, const void* a, const void* b, const void* c, const void* d,

@@ -27,6 +27,18 @@ namespace ca {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSeriesMax = 1.0f;
 
+// Where row r = bh*T + t of an activation in the [B,H,T,D] view (the output o or
+// its gradient dO) is stored: row r itself when the tensor is stored [B,H,T,D]
+// (bthd == 0), or row (b*T + t)*H + h when it is stored [B,T,H,D] (bthd != 0),
+// the layout the attention output projection reads.  q, k, v, the fp32 output
+// accumulator and the gradients dq, dk, dv are always [B,H,T,D].
+__host__ __device__ __forceinline__ size_t act_row(size_t r, long long T, long long H, int bthd) {
+  if (!bthd) return r;
+  const size_t bh = r / (size_t)T, t = r - bh * (size_t)T;
+  const size_t b = bh / (size_t)H, h = bh - b * (size_t)H;
+  return (b * (size_t)T + t) * (size_t)H + h;
+}
+
 // 2^x on the MUFU pipe (relative error about 2^-22; flushes subnormal results to 0).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -20,6 +20,7 @@ struct FwdArgs {
   int dtype;         // enum ca_dtype
   float inv_sqrt_d;  // float32(1/sqrt(D)), as the reference's D**-0.5 scalar
   cudaStream_t stream;
+  int o_bthd;        // o stored [B,T,H,D] instead of [B,H,T,D] (o_f32 stays [B,H,T,D])
 };
 
 struct BwdArgs {
@@ -39,6 +40,7 @@ struct BwdArgs {
   int dtype;
   float inv_sqrt_d;
   cudaStream_t stream;
+  int act_bthd;        // o and d_o stored [B,T,H,D] instead of [B,H,T,D] (o_f32 stays [B,H,T,D])
 };
 
 // Carved out of the caller's workspace (ca_capi.cu: workspace_layout).

@@ -52,7 +52,7 @@ template <typename T, int DP>
 __global__ void __launch_bounds__(NT)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const float* __restrict__ log_gain, T* __restrict__ o, float* __restrict__ o32,
-           float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d) {
+           float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d, int o_bthd) {
   pdl_wait();
   pdl_launch_dependents();
   using L = FwdSmem<DP>;
@@ -210,12 +210,13 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const float inv = 1.f / Z;
   const T* v0 = v + base;
   const T* vi = v + base + (size_t)i * D;
+  T* orow = o + act_row((size_t)bh * Tn + i, Tn, H, o_bthd) * D;
 #pragma unroll
   for (int x = 0; x < DQ; ++x) {
     const int d = quad + 4 * x;
     if (d < D) {
       const float y = (acc[x] + w0 * to_f32(v0[d]) + wi * to_f32(vi[d])) * inv;
-      o[base + (size_t)i * D + d] = from_f32<T>(y);
+      orow[d] = from_f32<T>(y);
       if (o32) o32[base + (size_t)i * D + d] = y;
     }
   }
@@ -256,7 +257,7 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
            const T* __restrict__ dout, const float* __restrict__ log_gain,
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            float* __restrict__ dq_acc, T* __restrict__ dk, T* __restrict__ dv,
-           float* __restrict__ gain_part, int BH, int H, int Tn, int D, float inv_sqrt_d) {
+           float* __restrict__ gain_part, int BH, int H, int Tn, int D, float inv_sqrt_d, int do_bthd) {
   pdl_wait();
   pdl_launch_dependents();
   using L = BwdSmem<DP>;
@@ -306,7 +307,7 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       const int rr = idx / DP, d = idx % DP, row = q0 + rr;
       const bool ok = row < Tn && d < D;
       Qs[rr * L::LD + d] = ok ? to_f32(q[base + (size_t)row * D + d]) : 0.f;
-      Os[rr * L::LD + d] = ok ? to_f32(dout[base + (size_t)row * D + d]) : 0.f;
+      Os[rr * L::LD + d] = ok ? to_f32(dout[act_row((size_t)bh * Tn + row, Tn, H, do_bthd) * D + d]) : 0.f;
     }
     if (tid < BQ) {
       const int row = q0 + tid;
@@ -488,14 +489,17 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 // D_i = dO_i . O_i  (one warp per row); O in the element type TO (dtype or its fp32 accumulator)
 template <typename TO, typename T>
 __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ dout,
-                              float* __restrict__ rowdot, size_t rows, int D) {
+                              float* __restrict__ rowdot, size_t rows, int D, int Tn, int H, int o_bthd,
+                              int do_bthd) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t row = (size_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float s = 0.f;
-  for (int d = lane; d < D; d += 32) s = fmaf(to_f32(o[row * D + d]), to_f32(dout[row * D + d]), s);
+  const TO* orow = o + act_row(row, Tn, H, o_bthd) * D;
+  const T* drow = dout + act_row(row, Tn, H, do_bthd) * D;
+  for (int d = lane; d < D; d += 32) s = fmaf(to_f32(orow[d]), to_f32(drow[d]), s);
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) rowdot[row] = s;
 }
@@ -503,9 +507,12 @@ __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ do
 // Backward preparation for D = 64, one pass: D_i = dO_i . O_i and zeros for the
 // fp32 dQ accumulator.  16 threads per row, 4 consecutive elements each
 // (16-byte O loads when O is fp32, 8-byte dO loads), 2 rows per warp.
-template <typename TO, typename T>
+// kOB / kDB: O / dO rows stored [B,T,H,D] (act_row); compile-time, so the usual
+// [B,H,T,D] case carries no index arithmetic.
+template <typename TO, typename T, bool kOB, bool kDB>
 __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ dout, float* __restrict__ rowdot,
-                              float* __restrict__ dq_acc, size_t rows, unsigned* __restrict__ counter) {
+                              float* __restrict__ dq_acc, size_t rows, unsigned* __restrict__ counter, int Tn,
+                              int H) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -515,19 +522,21 @@ __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ do
   float s = 0.f;
   if (row < rows) {
     const size_t base = row * 64 + 4 * part;
+    const size_t obase = (kOB ? act_row(row, Tn, H, 1) * 64 + 4 * part : base);
+    const size_t dbase = (kDB ? act_row(row, Tn, H, 1) * 64 + 4 * part : base);
     float ov[4], dv[4];
     if (sizeof(TO) == 4) {
-      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(o) + base);
+      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(o) + obase);
       ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
     } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) ov[u] = to_f32(o[base + u]);
+      for (int u = 0; u < 4; ++u) ov[u] = to_f32(o[obase + u]);
     }
     if (sizeof(T) == 4) {
-      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(dout) + base);
+      const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(dout) + dbase);
       dv[0] = x.x; dv[1] = x.y; dv[2] = x.z; dv[3] = x.w;
     } else {
-      const uint2 raw = *reinterpret_cast<const uint2*>(dout + base);
+      const uint2 raw = *reinterpret_cast<const uint2*>(dout + dbase);
       const T* dp = reinterpret_cast<const T*>(&raw);
 #pragma unroll
       for (int u = 0; u < 4; ++u) dv[u] = to_f32(dp[u]);
@@ -605,7 +614,7 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   const long long nqt = (a.T + BQ - 1) / BQ;
   return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
                     (const T*)a.v, a.log_gain, (T*)a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T,
-                    (int)a.D, a.inv_sqrt_d);
+                    (int)a.D, a.inv_sqrt_d, a.o_bthd);
 }
 
 template <typename T>
@@ -634,7 +643,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   return launch_pdl(kern, dim3((unsigned)(BH * nkt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
                     (const T*)a.v, (const T*)a.d_o, a.log_gain, a.row_stats, (const float*)w.rowdot, w.dq_acc,
                     (T*)a.dk, (T*)a.dv, a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T,
-                    (int)a.D, a.inv_sqrt_d);
+                    (int)a.D, a.inv_sqrt_d, a.act_bthd);
 }
 
 template <typename T>
@@ -643,9 +652,9 @@ static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
   const dim3 grid((unsigned)((rows + 7) / 8));
   if (a.o_f32)
     return launch_pdl(rowdot_kernel<float, T>, grid, dim3(256), 0, a.stream, (const float*)a.o_f32,
-                      (const T*)a.d_o, rowdot, rows, (int)a.D);
+                      (const T*)a.d_o, rowdot, rows, (int)a.D, (int)a.T, (int)a.H, 0, a.act_bthd);
   return launch_pdl(rowdot_kernel<T, T>, grid, dim3(256), 0, a.stream, (const T*)a.o, (const T*)a.d_o, rowdot,
-                    rows, (int)a.D);
+                    rows, (int)a.D, (int)a.T, (int)a.H, a.act_bthd, a.act_bthd);
 }
 
 template <typename T>
@@ -664,11 +673,15 @@ static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc, un
     return cudaMemsetAsync(dq_acc, 0, rows * a.D * sizeof(float), a.stream);
   }
   const unsigned blocks = (unsigned)((rows * 16 + 255) / 256);
-  if (a.o_f32)
-    return launch_pdl(prep64_kernel<float, T>, dim3(blocks), dim3(256), 0, a.stream, (const float*)a.o_f32,
-                      (const T*)a.d_o, rowdot, dq_acc, rows, counter);
-  return launch_pdl(prep64_kernel<T, T>, dim3(blocks), dim3(256), 0, a.stream, (const T*)a.o, (const T*)a.d_o,
-                    rowdot, dq_acc, rows, counter);
+  const dim3 g(blocks), b(256);
+  if (a.o_f32) {
+    auto k = a.act_bthd ? prep64_kernel<float, T, false, true> : prep64_kernel<float, T, false, false>;
+    return launch_pdl(k, g, b, 0, a.stream, (const float*)a.o_f32, (const T*)a.d_o, rowdot, dq_acc, rows, counter,
+                      (int)a.T, (int)a.H);
+  }
+  auto k = a.act_bthd ? prep64_kernel<T, T, true, true> : prep64_kernel<T, T, false, false>;
+  return launch_pdl(k, g, b, 0, a.stream, (const T*)a.o, (const T*)a.d_o, rowdot, dq_acc, rows, counter, (int)a.T,
+                    (int)a.H);
 }
 
 cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter) {

@@ -319,7 +319,8 @@ __device__ __forceinline__ int fwd_chunk_kind(int ch, int kb, int q0, int warp, 
 
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32, float* stats,
-                           int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d) {
+                           int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d, int H,
+                           int o_bthd) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = warp * 32 + lane;
@@ -456,7 +457,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   }
   z += z2.x + z2.y;
   const float inv = 1.f / z;
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + row * HD);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + act_row(row, Tn, H, o_bthd) * HD);
 #pragma unroll
   for (int c = 0; c < HD / 8; ++c) {
     uint32_t w[4];
@@ -484,7 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const void* __restrict__ vptr,
            const float* __restrict__ log_gain, void* __restrict__ optr, float* __restrict__ o32,
-           float* __restrict__ stats, int BH, int H, int Tn, float inv_sqrt_d) {
+           float* __restrict__ stats, int BH, int H, int Tn, float inv_sqrt_d, int o_bthd) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -532,7 +533,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d);
+    math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H, o_bthd);
   }
   tc_fence_before();
   __syncthreads();
@@ -676,10 +677,10 @@ __device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
 // math warps at this item's last tile, and this item's final dQ reduce waits until
 // the next item's first S/dP is issued: the next item's start overlaps this
 // item's epilogue.
-template <bool kBF16>
+template <bool kBF16, bool kDOB>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
                          const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int n_items,
-                         unsigned* counter, uint32_t tmem) {
+                         unsigned* counter, uint32_t tmem, int H) {
   volatile int* ab = &sm.abort_flag;
   const int lane = threadIdx.x & 31;
   const uint32_t id_s = make_idesc(BM, KH, kBF16, false, false);
@@ -708,7 +709,10 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   auto load_qdo = [&](int st, const Item& it, int t) {
     mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
     tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
-    tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
+    if (kDOB)   // dO stored [B][T][H][D]: map (D, H, T, B)
+      tma_load_4d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.bh % H, it.j0 + t * BM, it.bh / H);
+    else
+      tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
     q_pending[st] = true;
   };
   auto publish = [&](int w) {
@@ -1253,7 +1257,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   }
 }
 
-template <bool kBF16>
+template <bool kBF16, bool kDOB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -1301,7 +1305,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   pdl_launch_dependents();
 
   if (warp == NUM_MATH_WARPS) {
-    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, tmem);   // converged
+    producer<kBF16, kDOB>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, tmem,
+                          H);   // converged
     __syncwarp();
   } else {
     math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, n_items, tmem,
@@ -1351,6 +1356,23 @@ static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T
   return r == CUDA_SUCCESS;
 }
 
+// [B, T, H, D] 16-bit tensor viewed as (D, H, T, B), box = {64 (D), 1, box_rows, 1}: for
+// one (b, h) the same box_rows rows of 128 bytes as make_map's box, 128-byte swizzle, OOB -> 0
+static bool make_map_bthd(CUtensorMap* m, const void* base, long long B, long long H, long long T, long long D,
+                          bool bf16, unsigned box_rows = 128) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(D * 2), (cuuint64_t)(H * D * 2), (cuuint64_t)(T * H * D * 2)};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // [BH, T, 64] f32 accumulator, box = {32, 128, 1} (128-byte rows), 128-byte swizzle
 static bool make_map_f32(CUtensorMap* m, void* base, long long BH, long long T) {
   EncodeTiledFn enc = encode_fn();
@@ -1392,7 +1414,8 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   if (e != cudaSuccess) return e;
   const long long nqt = (a.T + fwd::BM - 1) / fwd::BM;
   return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(fwd::NUM_THREADS), fwd::kSmemBytes, a.stream, mq, mk, mv,
-                    a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
+                    a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d,
+                    a.o_bthd);
 }
 
 cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a) : launch_fwd<false>(a); }
@@ -1401,13 +1424,15 @@ template <bool kBF16>
 static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   const long long BH = a.B * a.H;
   CUtensorMap mq, mk, mv, mdo, mdq;
-  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM) ||
+  const bool do_ok = a.act_bthd ? make_map_bthd(&mdo, a.d_o, a.B, a.H, a.T, a.D, kBF16, bwd::BM)
+                                : make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM);
+  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !do_ok ||
       !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH) ||
       !make_map_f32(&mdq, w.dq_acc, BH, a.T))
     return cudaErrorInvalidValue;
   cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc, w.counter);
   if (e != cudaSuccess) return e;
-  auto kern = bwd::bwd_kernel<kBF16>;
+  auto kern = a.act_bthd ? bwd::bwd_kernel<kBF16, true> : bwd::bwd_kernel<kBF16, false>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;

@@ -11,7 +11,8 @@ initialised with std 0.02/sqrt(2 n_layers)).
 ``attention_fn`` defaults to the CUDA operator; tests on machines without a GPU
 pass a CPU stand-in with the same signature.  On CUDA the attention block's
 input side is one native kernel (``rope.rope_qkv``: QKV unpacking fused with the
-rotary embedding) and each norm is one native kernel forward (``rmsnorm``).
+rotary embedding), the attention output is stored in the projection's input
+order, and each norm is one native kernel forward (``rmsnorm``).
 """
 from __future__ import annotations
 
@@ -101,8 +102,12 @@ class ContinuumSelfAttention(nn.Module):
     def forward(self, x):
         B, T, C = x.shape
         q, k, v = rope_qkv(self.qkv(x), self.heads, self.rope_theta)
-        y = self.attention_fn(q, k, v, self.log_qk_gain, self.ca_query_tile)
-        return self.out(y.transpose(1, 2).contiguous().reshape(B, T, C))
+        if self.attention_fn is continuum_attention:
+            # the operator stores y [B,T,H,D]: the projection's input below is a view of it
+            y = continuum_attention(q, k, v, self.log_qk_gain, self.ca_query_tile, out_layout="bthd")
+        else:
+            y = self.attention_fn(q, k, v, self.log_qk_gain, self.ca_query_tile)
+        return self.out(y.transpose(1, 2).reshape(B, T, C))
 
 
 class GELUMLP(nn.Module):

@@ -66,8 +66,14 @@ enum ca_status {
 enum ca_impl {
   CA_IMPL_AUTO = 0,   /* tcgen05 tensor-core kernels where they apply, else SIMT */
   CA_IMPL_SIMT = 1,   /* CUDA-core kernels: every dtype, D <= 128, fp32 arithmetic */
-  CA_IMPL_TCGEN05 = 2 /* sm_100a tcgen05/TMEM/TMA kernels: bf16/f16, D in {32,64,128} */
+  CA_IMPL_TCGEN05 = 2 /* sm_100a tcgen05/TMEM/TMA kernels: bf16/f16, D = 64 */
 };
+
+/* Storage order of the activations o (forward output, backward input) and d_o
+ * (ca_forward_ex / ca_backward_ex): [B,H,T,D] like q, k, v, or [B,T,H,D], the
+ * order in which a decoder's output projection reads the attention output.
+ * o_f32, q, k, v and the gradients dq, dk, dv are always [B,H,T,D]. */
+enum ca_layout { CA_LAYOUT_BHTD = 0, CA_LAYOUT_BTHD = 1 };
 
 /* Version of this ABI (CA_ABI_VERSION of the built library). */
 int ca_abi_version(void);
@@ -93,6 +99,15 @@ int ca_forward(const void* q, const void* k, const void* v, const float* log_gai
                int64_t B, int64_t H, int64_t T, int64_t D,
                int dtype, int impl, void* stream);
 
+/* ca_forward with o written in the given ca_layout.  CA_LAYOUT_BTHD replaces the
+ * copy the reference decoder makes of the attention output before its output
+ * projection (y.transpose(1, 2).contiguous(), cuda/continuum_attention.py:854):
+ * o [B][T][H][D] is that projection's input as it stands. */
+int ca_forward_ex(const void* q, const void* k, const void* v, const float* log_gain,
+                  void* o, float* o_f32, float* row_stats,
+                  int64_t B, int64_t H, int64_t T, int64_t D,
+                  int dtype, int impl, int layout, void* stream);
+
 /* Bytes of scratch space ca_backward needs for this shape (>= 0). */
 size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, int dtype);
 
@@ -116,6 +131,16 @@ int ca_backward(const void* q, const void* k, const void* v, const void* o, cons
                 void* workspace, size_t workspace_bytes,
                 int64_t B, int64_t H, int64_t T, int64_t D,
                 int dtype, int impl, void* stream);
+
+/* ca_backward with o and d_o read in the given ca_layout (the layout ca_forward_ex
+ * wrote o in; with CA_LAYOUT_BTHD d_o is the output projection's input gradient as
+ * it stands, [B][T][H][D], instead of its transposed copy). */
+int ca_backward_ex(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                   const void* d_o, const float* log_gain, const float* row_stats,
+                   void* dq, void* dk, void* dv, float* dlog_gain,
+                   void* workspace, size_t workspace_bytes,
+                   int64_t B, int64_t H, int64_t T, int64_t D,
+                   int dtype, int impl, int layout, void* stream);
 
 /*
  * Backward without caller-provided scratch.  No counterpart in the reference
