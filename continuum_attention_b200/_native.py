@@ -42,6 +42,8 @@ SIGNATURES = {
     "ca_rmsnorm_workspace_size": (_sz, [_i64, _i64]),
     "ca_rmsnorm_forward": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _int, _vp]),
     "ca_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _int, _vp]),
+    "ca_add_rmsnorm_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "ca_add_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _vp]),
 }
 
 _lock = threading.Lock()

@@ -315,6 +315,51 @@ int ca_rmsnorm_backward(const void* x, const float* w, const void* dy, const flo
   return ok();
 }
 
+int ca_add_rmsnorm_forward(const float* x, const void* r, const float* w, float* x_new, void* y, float* rstd,
+                           int64_t rows, int64_t D, float eps, void* stream) {
+  int st = check_norm("ca_add_rmsnorm_forward", rows, D, CA_DTYPE_F32, CA_DTYPE_BF16);
+  if (st != CA_OK) return st;
+  if (!(eps >= 0.f)) return fail(CA_ERR_INVALID_ARGUMENT, "ca_add_rmsnorm_forward: eps must be >= 0");
+  g_last_launches = 0;
+  if (rows == 0) return ok();
+  if (!x || !r || !w || !x_new || !y || !rstd)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_add_rmsnorm_forward: null pointer");
+  if (!all_aligned16({x, r, w, x_new, y, rstd}))
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_add_rmsnorm_forward: buffers must be 16-byte aligned");
+  cudaError_t e = ca::norm::add_forward(x, r, w, x_new, y, rstd, rows, D, eps, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_add_rmsnorm_forward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
+int ca_add_rmsnorm_backward(const float* x_new, const float* w, const void* dy, const float* rstd,
+                            const float* dx_new, float* dx, void* dr, float* dw, void* workspace,
+                            size_t workspace_bytes, int64_t rows, int64_t D, void* stream) {
+  int st = check_norm("ca_add_rmsnorm_backward", rows, D, CA_DTYPE_F32, CA_DTYPE_BF16);
+  if (st != CA_OK) return st;
+  g_last_launches = 0;
+  if (rows == 0) {
+    if (dw && D > 0) {
+      cudaError_t e = cudaMemsetAsync(dw, 0, (size_t)D * sizeof(float), (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "ca_add_rmsnorm_backward memset");
+    }
+    return ok();
+  }
+  if (!x_new || !w || !dy || !rstd || !dx || !dr || !dw || !workspace)
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_add_rmsnorm_backward: null pointer");
+  if (!all_aligned16({x_new, w, dy, rstd, dx_new, dx, dr, dw, workspace}))
+    return fail(CA_ERR_INVALID_ARGUMENT, "ca_add_rmsnorm_backward: buffers must be 16-byte aligned");
+  const size_t need = ca_rmsnorm_workspace_size(rows, D);
+  if (workspace_bytes < need)
+    return fail(CA_ERR_WORKSPACE, "ca_add_rmsnorm_backward: workspace of %zu bytes, %zu needed", workspace_bytes,
+                need);
+  cudaError_t e = ca::norm::add_backward(x_new, w, dy, rstd, dx_new, dx, dr, dw, (float*)workspace, rows, D,
+                                         (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_add_rmsnorm_backward launch");
+  g_last_launches = 2;
+  return ok();
+}
+
 int ca_selftest_wait_timeout(int64_t limit_us, void* stream) {
   if (limit_us < 1 || limit_us > 10000000)
     return fail(CA_ERR_INVALID_ARGUMENT, "ca_selftest_wait_timeout: limit_us=%lld outside [1, 1e7]",

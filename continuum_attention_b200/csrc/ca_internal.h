@@ -126,6 +126,13 @@ cudaError_t backward(const void* x, const float* w, const void* dy, const float*
                      float* dw_part, long long rows, long long D, int x_dtype, int y_dtype, cudaStream_t s);
 // floats of scratch backward needs (per-block partials of dw)
 size_t workspace_floats(long long rows, long long D);
+// residual add fused with the norm: x_new = x + r (x, x_new float32, r bfloat16),
+// y = norm(x_new) in bfloat16; backward gives dx = g_xnew + dnorm (float32) and
+// dr = the same in bfloat16 (g_xnew may be null: zero); same workspace as backward.
+cudaError_t add_forward(const float* x, const void* r, const float* w, float* xn, void* y, float* rstd,
+                        long long rows, long long D, float eps, cudaStream_t s);
+cudaError_t add_backward(const float* xn, const float* w, const void* dy, const float* rstd, const float* gxn,
+                         float* dx, void* dr, float* dw, float* dw_part, long long rows, long long D, cudaStream_t s);
 }  // namespace norm
 
 cudaError_t read_device_status(int* out, bool reset);

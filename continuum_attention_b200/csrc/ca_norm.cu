@@ -188,6 +188,118 @@ __global__ void __launch_bounds__(RW * 32) dw_reduce_kernel(const float* __restr
   }
 }
 
+// Residual add fused with the norm that follows it in a pre-norm block:
+//   x_new = x + r,  y = w * x_new * rsqrt(mean(x_new^2) + eps)
+// (x, x_new float32; r, y bfloat16: the residual stream and the branch output /
+// next projection input under bf16 autocast).  Saves the separate add kernel and
+// the norm's re-read of x_new.
+template <int NC>
+__global__ void __launch_bounds__(WARPS * 32) add_fwd_kernel(const float* __restrict__ x,
+                                                             const __nv_bfloat16* __restrict__ r,
+                                                             const float* __restrict__ w, float* __restrict__ xn,
+                                                             __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                             long long rows, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
+  constexpr int D = 128 * NC;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[NC][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    float xv[4], rv[4];
+    const long long off = row * D + 128 * c + 4 * lane;
+    load4<float>(x + off, xv);
+    load4<__nv_bfloat16>(r + off, rv);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[c][u] = xv[u] + rv[u];
+      ss = fmaf(v[c][u], v[c][u], ss);
+    }
+    store4<float>(xn + off, v[c]);
+  }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss * (1.f / D) + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    float wv[4], o[4];
+    load4<float>(w + 128 * c + 4 * lane, wv);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) o[u] = wv[u] * (v[c][u] * rs);
+    store4<__nv_bfloat16>(y + row * D + 128 * c + 4 * lane, o);
+  }
+  if (lane == 0) rstd[row] = rs;
+}
+
+// Backward of add_fwd_kernel: with t = g_xnew + (the norm's input gradient), the
+// gradients of x (float32) and of r (bfloat16) are both t; dw as in bwd_kernel.
+// kG: g_xnew is given (x_new is used further on); otherwise it is zero.
+template <int NC, bool kG>
+__global__ void __launch_bounds__(WARPS * 32) add_bwd_kernel(const float* __restrict__ xn,
+                                                             const float* __restrict__ w,
+                                                             const __nv_bfloat16* __restrict__ dy,
+                                                             const float* __restrict__ rstd,
+                                                             const float* __restrict__ gxn, float* __restrict__ dx,
+                                                             __nv_bfloat16* __restrict__ dr,
+                                                             float* __restrict__ dw_part, long long rows) {
+  pdl_wait();
+  pdl_launch_dependents();
+  constexpr int D = 128 * NC;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[NC][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[c][u] = 0.f;
+  for (long long row = (long long)blockIdx.x * WARPS + warp; row < rows; row += (long long)gridDim.x * WARPS) {
+    const float rs = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float xv[4], dv[4], wv[4];
+      const long long off = row * D + 128 * c + 4 * lane;
+      load4<float>(xn + off, xv);
+      load4<__nv_bfloat16>(dy + off, dv);
+      load4<float>(w + 128 * c + 4 * lane, wv);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dot = fmaf(dv[u] * wv[u], xv[u] * rs, dot);
+    }
+    const float mean = warp_sum(dot) * (1.f / D);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float xv[4], dv[4], wv[4], gv[4], o[4];
+      const long long off = row * D + 128 * c + 4 * lane;
+      load4<float>(xn + off, xv);
+      load4<__nv_bfloat16>(dy + off, dv);
+      load4<float>(w + 128 * c + 4 * lane, wv);
+      if (kG) load4<float>(gxn + off, gv);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float xh = xv[u] * rs;
+        const float nd = rs * fmaf(-xh, mean, dv[u] * wv[u]);
+        o[u] = kG ? gv[u] + nd : nd;
+        acc[c][u] = fmaf(dv[u], xh, acc[c][u]);
+      }
+      store4<float>(dx + off, o);
+      store4<__nv_bfloat16>(dr + off, o);
+    }
+  }
+  __shared__ float part[WARPS][128 * NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) part[warp][128 * c + 4 * lane + u] = acc[c][u];
+  __syncthreads();
+  for (int col = threadIdx.x; col < D; col += WARPS * 32) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < WARPS; ++k) s += part[k][col];
+    dw_part[(size_t)blockIdx.x * D + col] = s;
+  }
+}
+
 int backward_blocks(long long rows) {
   const long long need = (rows + WARPS - 1) / WARPS;
   const long long cap = (long long)num_sms_cached() * BWD_BLOCKS_PER_SM;
@@ -254,6 +366,49 @@ cudaError_t backward(const void* x, const float* w, const void* dy, const float*
   if (x_dtype == 1 && y_dtype == 1)
     return bwd_nc<__nv_bfloat16, __nv_bfloat16>(nc, x, w, dy, rstd, dx, dw, dw_part, rows, s);
   return bwd_nc<__nv_bfloat16, float>(nc, x, w, dy, rstd, dx, dw, dw_part, rows, s);
+}
+
+template <int NC>
+static cudaError_t add_fwd_t(const float* x, const void* r, const float* w, float* xn, void* y, float* rstd,
+                             long long rows, float eps, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((rows + WARPS - 1) / WARPS);
+  return launch_pdl(add_fwd_kernel<NC>, dim3(blocks), dim3(WARPS * 32), 0, s, x, (const __nv_bfloat16*)r, w, xn,
+                    (__nv_bfloat16*)y, rstd, rows, eps);
+}
+
+template <int NC>
+static cudaError_t add_bwd_t(const float* xn, const float* w, const void* dy, const float* rstd, const float* gxn,
+                             float* dx, void* dr, float* dw, float* dw_part, long long rows, cudaStream_t s) {
+  const int nb = backward_blocks(rows);
+  cudaError_t e = gxn ? launch_pdl(add_bwd_kernel<NC, true>, dim3(nb), dim3(WARPS * 32), 0, s, xn, w,
+                                   (const __nv_bfloat16*)dy, rstd, gxn, dx, (__nv_bfloat16*)dr, dw_part, rows)
+                      : launch_pdl(add_bwd_kernel<NC, false>, dim3(nb), dim3(WARPS * 32), 0, s, xn, w,
+                                   (const __nv_bfloat16*)dy, rstd, gxn, dx, (__nv_bfloat16*)dr, dw_part, rows);
+  if (e != cudaSuccess) return e;
+  constexpr int D = 128 * NC;
+  return launch_pdl(dw_reduce_kernel, dim3((D + 31) / 32), dim3(RW * 32), 0, s, (const float*)dw_part, dw, nb, D);
+}
+
+cudaError_t add_forward(const float* x, const void* r, const float* w, float* xn, void* y, float* rstd,
+                        long long rows, long long D, float eps, cudaStream_t s) {
+  switch (D / 128) {
+    case 1: return add_fwd_t<1>(x, r, w, xn, y, rstd, rows, eps, s);
+    case 2: return add_fwd_t<2>(x, r, w, xn, y, rstd, rows, eps, s);
+    case 4: return add_fwd_t<4>(x, r, w, xn, y, rstd, rows, eps, s);
+    case 8: return add_fwd_t<8>(x, r, w, xn, y, rstd, rows, eps, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t add_backward(const float* xn, const float* w, const void* dy, const float* rstd, const float* gxn,
+                         float* dx, void* dr, float* dw, float* dw_part, long long rows, long long D, cudaStream_t s) {
+  switch (D / 128) {
+    case 1: return add_bwd_t<1>(xn, w, dy, rstd, gxn, dx, dr, dw, dw_part, rows, s);
+    case 2: return add_bwd_t<2>(xn, w, dy, rstd, gxn, dx, dr, dw, dw_part, rows, s);
+    case 4: return add_bwd_t<4>(xn, w, dy, rstd, gxn, dx, dr, dw, dw_part, rows, s);
+    case 8: return add_bwd_t<8>(xn, w, dy, rstd, gxn, dx, dr, dw, dw_part, rows, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 size_t workspace_floats(long long rows, long long D) { return (size_t)backward_blocks(rows) * (size_t)D; }

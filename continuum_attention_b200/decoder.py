@@ -25,6 +25,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import continuum_attention
+from .rmsnorm import add_rms_norm, add_supported
 from .rmsnorm import rms_norm as native_rms_norm
 from .rmsnorm import supported as native_rms_norm_supported
 from .rope import apply_rope_torch, rope_qkv
@@ -156,16 +157,33 @@ class ContinuumDecoderLM(nn.Module):
         elif isinstance(m, nn.Embedding):
             nn.init.normal_(m.weight, mean=0.0, std=0.02)
 
+    @staticmethod
+    def _add_norm(x, r, norm):
+        """(x + r, norm(x + r)): one native kernel when the residual stream is float32
+        and the branch output bfloat16 (bf16 autocast on CUDA), else the two steps."""
+        if add_supported(x, r) and torch.is_autocast_enabled("cuda") and \
+                torch.get_autocast_dtype("cuda") == torch.bfloat16:
+            return add_rms_norm(x, r, norm.weight, norm.eps)
+        x = x + r
+        return x, norm(x)
+
     def forward(self, input_ids, targets=None):
         if input_ids.dim() != 2 or input_ids.shape[1] > self.cfg.block_size:
             raise ValueError("Input must be [B,T] with T<=block_size")
         x = self.byte_emb(input_ids)
-        for block in self.blocks:
-            if self.cfg.grad_checkpointing and self.training:
+        if self.cfg.grad_checkpointing and self.training:
+            for block in self.blocks:
                 x = torch.utils.checkpoint.checkpoint(block, x, use_reentrant=False)
-            else:
-                x = block(x)
-        logits = self.lm_head(self.norm_f(x))
+            h = self.norm_f(x)
+        else:
+            # the blocks' residual adds run together with the norm that follows each
+            # (the next block's norm1, or norm_f after the last block)
+            h = self.blocks[0].norm1(x)
+            for i, block in enumerate(self.blocks):
+                x, h = self._add_norm(x, block.attn(h), block.norm2)
+                nxt = self.blocks[i + 1].norm1 if i + 1 < len(self.blocks) else self.norm_f
+                x, h = self._add_norm(x, block.mlp(h), nxt)
+        logits = self.lm_head(h)
         out = {"logits": logits}
         if targets is not None:
             out["loss"] = F.cross_entropy(logits[:, :-1, :].reshape(-1, self.cfg.vocab_size),

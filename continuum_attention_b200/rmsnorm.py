@@ -72,3 +72,64 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype=None) 
         raise ValueError(f"native rms_norm covers CUDA float32/bfloat16 tensors with last dim in {_DIMS}; "
                          f"got {x.device} {x.dtype} -> {out_dtype}, last dim {x.shape[-1]}")
     return RMSNormFunction.apply(x, weight, eps, out_dtype)
+
+
+class AddRMSNormFunction(torch.autograd.Function):
+    """(x_new, y) = (x + r, rms_norm(x + r)) with x float32 and r, y bfloat16."""
+
+    @staticmethod
+    def forward(ctx, x, r, weight, eps: float):
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D).contiguous()
+        r2 = r.reshape(-1, D).contiguous()
+        rows = x2.shape[0]
+        w = weight.detach().to(torch.float32).contiguous()
+        xn = torch.empty_like(x2)
+        y = torch.empty(x2.shape, dtype=torch.bfloat16, device=x.device)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        lib = _native.lib()
+        with torch.cuda.device(x.device):
+            st = lib.ca_add_rmsnorm_forward(ctypes_ptr(x2), ctypes_ptr(r2), ctypes_ptr(w), ctypes_ptr(xn),
+                                            ctypes_ptr(y), ctypes_ptr(rstd), rows, D, float(eps),
+                                            torch.cuda.current_stream(x.device).cuda_stream)
+        _native.check("ca_add_rmsnorm_forward", st)
+        ctx.save_for_backward(xn, w, rstd)
+        ctx.shape = x.shape
+        ctx.weight_dtype = weight.dtype
+        return xn.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, g_xn, g_y):
+        xn, w, rstd = ctx.saved_tensors
+        rows, D = xn.shape
+        dy = (torch.zeros_like(xn, dtype=torch.bfloat16) if g_y is None
+              else g_y.reshape(-1, D).to(torch.bfloat16).contiguous())
+        gx = None if g_xn is None else g_xn.reshape(-1, D).to(torch.float32).contiguous()
+        dx = torch.empty_like(xn)
+        dr = torch.empty(xn.shape, dtype=torch.bfloat16, device=xn.device)
+        dw = torch.empty(D, dtype=torch.float32, device=xn.device)
+        lib = _native.lib()
+        ws = torch.empty(max(int(lib.ca_rmsnorm_workspace_size(rows, D)), 16), dtype=torch.uint8, device=xn.device)
+        with torch.cuda.device(xn.device):
+            st = lib.ca_add_rmsnorm_backward(ctypes_ptr(xn), ctypes_ptr(w), ctypes_ptr(dy), ctypes_ptr(rstd),
+                                             None if gx is None else ctypes_ptr(gx), ctypes_ptr(dx), ctypes_ptr(dr),
+                                             ctypes_ptr(dw), ws.data_ptr(), ws.numel(), rows, D,
+                                             torch.cuda.current_stream(xn.device).cuda_stream)
+        _native.check("ca_add_rmsnorm_backward", st)
+        return dx.view(ctx.shape), dr.view(ctx.shape), dw.to(ctx.weight_dtype), None
+
+
+def add_supported(x: torch.Tensor, r: torch.Tensor) -> bool:
+    """True when the fused residual add + norm covers the call: CUDA, x float32,
+    r bfloat16 of the same shape, last dim in 128/256/512/1024."""
+    return (x.is_cuda and r.is_cuda and x.dtype == torch.float32 and r.dtype == torch.bfloat16
+            and x.shape == r.shape and x.shape[-1] in _DIMS)
+
+
+def add_rms_norm(x: torch.Tensor, r: torch.Tensor, weight: torch.Tensor, eps: float):
+    """(x + r, rms_norm(x + r)) in one native kernel; the normalised output is
+    bfloat16.  Raises when ``add_supported`` is false."""
+    if not add_supported(x, r):
+        raise ValueError("native add_rms_norm covers CUDA float32 x with bfloat16 r of the same shape and last "
+                         f"dim in {_DIMS}; got {x.dtype}/{r.dtype} {tuple(x.shape)}/{tuple(r.shape)}")
+    return AddRMSNormFunction.apply(x, r, weight, eps)

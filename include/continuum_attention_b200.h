@@ -203,8 +203,26 @@ int ca_rmsnorm_backward(const void* x, const float* w, const void* dy, const flo
                         void* workspace, size_t workspace_bytes, int64_t rows, int64_t D, int x_dtype, int y_dtype,
                         void* stream);
 
-/* Number of kernels the last successful ca_forward / ca_backward /
- * ca_rope_qkv_* / ca_rmsnorm_* call on this thread enqueued (memsets
+/*
+ * The residual add before a pre-norm block's norm, fused with it: x_new = x + r,
+ * y = w * x_new * rsqrt(mean(x_new^2) + eps) (the reference block's
+ * `x = x + self.attn(...)` / `x + self.mlp(...)` followed by the next RMSNorm,
+ * cuda/continuum_attention.py:815-821 and the block's forward).  x, x_new float32
+ * (the residual stream), r and y bfloat16 (a branch output and the next
+ * projection's input under bf16 autocast), w float32 [D], rstd float32 [rows];
+ * D in {128, 256, 512, 1024}.  The backward takes the gradient of y (dy,
+ * bfloat16) and of x_new where it is used further on (dx_new, float32, NULL for
+ * none), and writes dx (float32) and dr (bfloat16), both equal to dx_new plus the
+ * norm's input gradient, and dw; scratch as ca_rmsnorm_workspace_size().
+ */
+int ca_add_rmsnorm_forward(const float* x, const void* r, const float* w, float* x_new, void* y, float* rstd,
+                           int64_t rows, int64_t D, float eps, void* stream);
+int ca_add_rmsnorm_backward(const float* x_new, const float* w, const void* dy, const float* rstd,
+                            const float* dx_new, float* dx, void* dr, float* dw, void* workspace,
+                            size_t workspace_bytes, int64_t rows, int64_t D, void* stream);
+
+/* Number of kernels the last successful ca_forward / ca_backward //* Number of kernels the last successful ca_forward / ca_backward /
+ * ca_rope_qkv_* / ca_rmsnorm_* / ca_add_rmsnorm_* call on this thread enqueued (memsets
  * excluded).  Diagnostic for launch accounting. */
 int ca_last_launch_count(void);
 

@@ -75,3 +75,33 @@ def test_decoder_block_norm_matches_torch_rms_norm():
     assert y.dtype == torch.bfloat16
     ref = torch.nn.functional.rms_norm(x, (1024,), norm.weight, norm.eps).to(torch.bfloat16)
     assert (y.float() - ref.float()).abs().max().item() <= 2 ** -7 * ref.float().abs().max().item()
+
+
+@pytest.mark.parametrize("D", [128, 1024])
+@pytest.mark.parametrize("use_xnew", [True, False])
+def test_add_rms_norm_matches_float64(D, use_xnew):
+    from continuum_attention_b200.rmsnorm import add_rms_norm
+    g = torch.Generator().manual_seed(100 + D)
+    x = torch.randn(2, 300, D, generator=g).to(DEV)
+    r = (torch.randn(2, 300, D, generator=g) * 0.5).to(DEV, torch.bfloat16)
+    w = (1 + 0.3 * torch.randn(D, generator=g)).to(DEV)
+    gy = torch.randn(x.shape, generator=g).to(DEV, torch.bfloat16)
+    gx = torch.randn(x.shape, generator=g).to(DEV)
+    eps = 1e-6
+    xs, rs, ws = (t.detach().clone().requires_grad_(True) for t in (x, r, w))
+    xn, y = add_rms_norm(xs, rs, ws, eps)
+    assert xn.dtype == torch.float32 and y.dtype == torch.bfloat16
+    loss = (y.float() * gy.float()).sum() + ((xn * gx).sum() if use_xnew else 0.0)
+    dx, dr, dw = torch.autograd.grad(loss, (xs, rs, ws))
+
+    x64, r64, w64 = (t.double().requires_grad_(True) for t in (x, r, w))
+    xn64 = x64 + r64
+    y64 = _reference(xn64, w64, eps)
+    loss64 = (y64 * gy.double()).sum() + ((xn64 * gx.double()).sum() if use_xnew else 0.0)
+    rdx, rdr, rdw = torch.autograd.grad(loss64, (x64, r64, w64))
+    assert (xn.double() - xn64.detach()).abs().max().item() < 1e-5
+    err_y = ((y.double() - y64.detach()).abs() / y64.detach().abs().clamp_min(1e-3)).max().item()
+    assert err_y < 2 ** -7, err_y
+    for name, a, b, tol in (("dx", dx, rdx, 1e-4), ("dr", dr, rdr, 1e-2), ("dw", dw, rdw, 1e-4)):
+        err = ((a.double() - b).abs().max() / b.abs().max()).item()
+        assert err < tol, (name, err)
