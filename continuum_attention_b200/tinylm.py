@@ -211,3 +211,42 @@ class TinyLMTrainer:
         self.target.copy_(target, non_blocking=True)
         self.graph.replay()
         return self.loss
+
+
+def _main(argv=None):
+    """Training-step throughput of TinyLM (fixed-tau variant P by default, fp32 as the
+    reference trains it) on one GPU, synthetic bytes, the step as one CUDA graph:
+    ``python -m continuum_attention_b200.tinylm [--steps K] [--seq-len T]``.
+    Prints one JSON line."""
+    import argparse
+    import json
+    p = argparse.ArgumentParser(description=_main.__doc__)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--seq-len", type=int, default=192)
+    p.add_argument("--variant", default="P")
+    args = p.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(1729)
+    model = TinyLM(variant=args.variant, seq_len=args.seq_len).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(1729)
+    batch = torch.randint(0, 256, (args.batch, args.seq_len + 1), generator=g).to(dev)
+    x, y = batch[:, :-1].contiguous(), batch[:, 1:].contiguous()
+    trainer = TinyLMTrainer(model, batch_size=args.batch, seq_len=args.seq_len)
+    for _ in range(5):
+        trainer.step(x, y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = trainer.step(x, y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    print(json.dumps({"metric": f"TinyLM-{args.variant} train tokens/s", "value": args.batch * args.seq_len / (ms * 1e-3),
+                      "ms_per_step": ms, "steps": args.steps, "seq_len": args.seq_len, "loss": float(loss.item()),
+                      "params": parameters(model)}))
+
+
+if __name__ == "__main__":
+    _main()
