@@ -28,13 +28,16 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import continuum_attention
+from .rmsnorm import rms_norm as native_rms_norm
+from .rmsnorm import supported as rms_norm_supported
 
 CONTINUOUS = ("P", "R", "S", "H")
 SOFTMAX = ("A", "B", "F", "G")
 
 
 class RMSNorm(nn.Module):
-    """x * rsqrt(mean(x^2) + eps) * weight (architecture.py:21-28), one fused kernel."""
+    """x * rsqrt(mean(x^2) + eps) * weight (architecture.py:21-28): the native kernel
+    (``rmsnorm.rms_norm``) on CUDA at the widths it covers, else torch's fused one."""
 
     def __init__(self, width: int, eps: float = 1e-5):
         super().__init__()
@@ -42,6 +45,8 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
+        if rms_norm_supported(x, x.dtype):
+            return native_rms_norm(x, self.weight, self.eps, x.dtype)
         return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 
@@ -78,7 +83,10 @@ class CausalAttention(nn.Module):
         B, T, _ = x.shape
         q, k, v = self.qkv(x).chunk(3, dim=-1)
         q, k, v = (t.reshape(B, T, self.heads, self.head_dim).transpose(1, 2) for t in (q, k, v))
-        if self.continuous:
+        if self.continuous and self.attention_fn is continuum_attention:
+            # stored [B,T,H,D]: the output projection below reads it without a copy
+            y = continuum_attention(q, k, v, self._log_gain(x.device), 64, out_layout="bthd")
+        elif self.continuous:
             y = self.attention_fn(q, k, v, self._log_gain(x.device), 64)
         else:
             if self.variant == "B":
@@ -86,7 +94,7 @@ class CausalAttention(nn.Module):
             elif self.variant in ("F", "G"):
                 q = q * self.log_qk_gain.exp().view(1, -1, 1, 1)
             y = F.scaled_dot_product_attention(q, k, v, is_causal=True, dropout_p=0.0)
-        return self.out(y.transpose(1, 2).contiguous().reshape(B, T, self.width))
+        return self.out(y.transpose(1, 2).reshape(B, T, self.width))
 
 
 class SwiGLU(nn.Module):
