@@ -32,39 +32,133 @@ constexpr int BQ = 64;
 constexpr int BK = 64;
 constexpr int NT = 256;
 
+// Shared tiles hold fp32 rows of stride DP + 4 floats: every row starts on a
+// 16-byte boundary (float4 access), and rows r and r+1 start 4 banks apart, so
+// one float4 column chunk read from 8 consecutive rows touches each bank once.
+//
+// The GEMM phases use register tiles of 4 rows x 4 keys (or 4 rows x DP/16
+// columns) fed by float4 shared-memory reads along the reduction index; each
+// sums its reduction index in increasing order, as a plain dot product does.
+
+// 4 consecutive elements as fp32 (one 16-byte load for fp32, 8-byte for 16-bit types)
+template <typename T> __device__ __forceinline__ float4 ld4(const T* p);
+template <> __device__ __forceinline__ float4 ld4<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+template <> __device__ __forceinline__ float4 ld4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <> __device__ __forceinline__ float4 ld4<__half>(const __half* p) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// 4 consecutive fp32 values stored as T (round to nearest)
+template <typename T> __device__ __forceinline__ void st4(T* p, float4 x);
+template <> __device__ __forceinline__ void st4<float>(float* p, float4 x) { *reinterpret_cast<float4*>(p) = x; }
+template <> __device__ __forceinline__ void st4<__nv_bfloat16>(__nv_bfloat16* p, float4 x) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(x.x, x.y), b = __floats2bfloat162_rn(x.z, x.w);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+template <> __device__ __forceinline__ void st4<__half>(__half* p, float4 x) {
+  const __half2 a = __floats2half2_rn(x.x, x.y), b = __floats2half2_rn(x.z, x.w);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+
+// Rows row0 .. row0+n-1 of one head into tile rows 0 .. n-1 (fp32, stride DP + 4).
+// Element (row, d) is src[off + row * rs + d]; rows outside [0, Tn) and columns
+// d >= D read as 0.  vec: D == DP and 4-element chunks of src are aligned.
+template <typename T, int DP>
+__device__ __forceinline__ void load_tile(float* dst, const T* __restrict__ src, size_t off, size_t rs, int row0,
+                                          int n, int Tn, int D, bool vec) {
+  constexpr int LD = DP + 4;
+  if (vec) {
+    constexpr int C4 = DP / 4;
+    for (int idx = threadIdx.x; idx < n * C4; idx += NT) {
+      const int rr = idx / C4, c = (idx - rr * C4) * 4, row = row0 + rr;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row >= 0 && row < Tn) x = ld4(src + off + (size_t)row * rs + c);
+      *reinterpret_cast<float4*>(dst + rr * LD + c) = x;
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < n * DP; idx += NT) {
+      const int rr = idx / DP, d = idx - rr * DP, row = row0 + rr;
+      dst[rr * LD + d] = (row >= 0 && row < Tn && d < D) ? to_f32(src[off + (size_t)row * rs + d]) : 0.f;
+    }
+  }
+}
+
+// CW consecutive floats of a shared row (16-byte aligned for CW % 4 == 0, 8-byte for CW == 2)
+template <int CW>
+__device__ __forceinline__ void lds_cols(float (&dst)[CW], const float* p) {
+  if constexpr (CW % 4 == 0) {
+#pragma unroll
+    for (int w = 0; w < CW; w += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(p + w);
+      dst[w] = x.x; dst[w + 1] = x.y; dst[w + 2] = x.z; dst[w + 3] = x.w;
+    }
+  } else {
+    static_assert(CW == 2, "DP must be 32, 64 or 128");
+    const float2 x = *reinterpret_cast<const float2*>(p);
+    dst[0] = x.x; dst[1] = x.y;
+  }
+}
+
+// CW consecutive outputs of one row: columns col0 .. col0+CW-1 of a D-wide row
+template <typename T, int CW>
+__device__ __forceinline__ void store_cols(T* row, int col0, const float (&x)[CW], int D, bool vec) {
+  if (vec && CW % 4 == 0) {
+#pragma unroll
+    for (int w = 0; w < CW; w += 4) st4<T>(row + col0 + w, make_float4(x[w], x[w + 1], x[w + 2], x[w + 3]));
+  } else {
+#pragma unroll
+    for (int w = 0; w < CW; ++w)
+      if (col0 + w < D) row[col0 + w] = from_f32<T>(x[w]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward
+
 template <int DP>
 struct FwdSmem {
-  static constexpr int LD = DP + 1;      // padded Q/K row
-  static constexpr int SLD = BK + 2;     // score row (keys j0..j0+63, padded)
-  static constexpr int PLD = BK + 1;     // P row
+  static constexpr int LD = DP + 4;      // Q / K / V' rows
+  static constexpr int SLD = BK + 4;     // score row (keys j0 .. j0+63), then its P row in place
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + BQ * LD;
   static constexpr int kV = kK + BK * LD;
-  static constexpr int kS = kV + BK * DP;
-  static constexpr int kP = kS + BQ * SLD;
-  static constexpr int kFirst = kP + BQ * PLD;
-  static constexpr int kDiag = kFirst + BQ;
-  static constexpr int kFloats = kDiag + BQ;
+  static constexpr int kS = kV + BK * LD;
+  static constexpr int kRow = kS + BQ * SLD;   // per-row alpha, first, diag, w0, wi, 1/Z
+  static constexpr int kFloats = kRow + 6 * BQ;
   static constexpr size_t bytes = sizeof(float) * kFloats;
 };
 
 template <typename T, int DP>
-__global__ void __launch_bounds__(NT)
+__global__ void __launch_bounds__(NT, 2)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const float* __restrict__ log_gain, T* __restrict__ o, float* __restrict__ o32,
-           float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d, int o_bthd) {
+           float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d, int o_bthd, int vec) {
   pdl_wait();
   pdl_launch_dependents();
   using L = FwdSmem<DP>;
-  constexpr int DQ = DP / 4;             // O columns per thread
-  extern __shared__ float smem[];
+  constexpr int LD = L::LD, SLD = L::SLD;
+  constexpr int CW = DP / 16;            // O columns per thread
+  extern __shared__ __align__(16) float smem[];
   float* Qs = smem + L::kQ;
   float* Ks = smem + L::kK;
   float* Vs = smem + L::kV;
   float* Ss = smem + L::kS;
-  float* Ps = smem + L::kP;
-  float* sFirst = smem + L::kFirst;
-  float* sDiag = smem + L::kDiag;
+  float* sAlpha = smem + L::kRow;
+  float* sFirst = sAlpha + BQ;
+  float* sDiag = sFirst + BQ;
+  float* sW0 = sDiag + BQ;
+  float* sWi = sW0 + BQ;
+  float* sInv = sWi + BQ;
 
   const int tid = threadIdx.x;
   const int nqt = (Tn + BQ - 1) / BQ;
@@ -75,34 +169,30 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const size_t base = (size_t)bh * Tn * D;
   const float scale = expf(log_gain[h]) * inv_sqrt_d;
 
-  for (int idx = tid; idx < BQ * DP; idx += NT) {
-    const int r = idx / DP, d = idx % DP, row = q0 + r;
-    Qs[r * L::LD + d] = (row < Tn && d < D) ? to_f32(q[base + (size_t)row * D + d]) : 0.f;
-  }
+  load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
 
-  // row-phase identity: 4 consecutive lanes share one query row
+  // row phase: 4 consecutive lanes share query row r, keys 16*quad .. +15
   const int r = tid >> 2, quad = tid & 3;
   const int lane = tid & 31;
   const int i = q0 + r;
   const bool row_ok = i < Tn;
   float m_run = -INFINITY, z_part = 0.f, bpend = 0.f, sprev = 0.f;
-  float acc[DQ];
+  // tile phases: rows 4ty .. 4ty+3; keys tx + 16b (S) or O columns tx*CW .. (P V')
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[4][CW];
 #pragma unroll
-  for (int x = 0; x < DQ; ++x) acc[x] = 0.f;
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int w = 0; w < CW; ++w) acc[a][w] = 0.f;
 
   const int last_row = min(q0 + BQ, Tn) - 1;
   const int nkt = last_row / BK + 1;
-  const int ty = tid >> 4, tx = tid & 15;
 
   for (int kt = 0; kt < nkt; ++kt) {
     const int j0 = kt * BK;
     __syncthreads();
-    for (int idx = tid; idx < BK * DP; idx += NT) {
-      const int c = idx / DP, d = idx % DP;
-      const int key = j0 + c, vkey = j0 - 1 + c;
-      Ks[c * L::LD + d] = (key < Tn && d < D) ? to_f32(k[base + (size_t)key * D + d]) : 0.f;
-      Vs[c * DP + d] = (vkey >= 0 && vkey < Tn && d < D) ? to_f32(v[base + (size_t)vkey * D + d]) : 0.f;
-    }
+    load_tile<T, DP>(Ks, k, base, D, j0, BK, Tn, D, vec);
+    load_tile<T, DP>(Vs, v, base, D, j0 - 1, BK, Tn, D, vec);   // V' row c = key j0-1+c
     __syncthreads();
     {
       float sacc[4][4];
@@ -110,41 +200,54 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
-#pragma unroll 4
-      for (int d = 0; d < DP; ++d) {
-        float qa[4], kb[4];
+#pragma unroll 2
+      for (int d = 0; d < DP; d += 4) {
+        float4 qa[4], kb[4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) qa[a] = Qs[(ty + 16 * a) * L::LD + d];
+        for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(Qs + (4 * ty + a) * LD + d);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) kb[b] = Ks[(tx + 16 * b) * L::LD + d];
+        for (int b = 0; b < 4; ++b) kb[b] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * b) * LD + d);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int b = 0; b < 4; ++b) sacc[a][b] = fmaf(qa[a], kb[b], sacc[a][b]);
+          for (int b = 0; b < 4; ++b) {
+            float s = fmaf(qa[a].x, kb[b].x, sacc[a][b]);
+            s = fmaf(qa[a].y, kb[b].y, s);
+            s = fmaf(qa[a].z, kb[b].z, s);
+            sacc[a][b] = fmaf(qa[a].w, kb[b].w, s);
+          }
       }
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) Ss[(ty + 16 * a) * L::SLD + tx + 16 * b] = sacc[a][b] * scale;
+        for (int b = 0; b < 4; ++b) Ss[(4 * ty + a) * SLD + tx + 16 * b] = sacc[a][b] * scale;
     }
     __syncthreads();
     {
-      const float* srow = Ss + r * L::SLD;   // srow[c] = score of key j0 + c
+      float* srow = Ss + r * SLD;   // srow[c] = score of key j0 + c; becomes P[c] (key j0-1+c)
       const int nvis = row_ok ? min(max(i - j0 + 1, 0), BK) : 0;
       const int c0 = 16 * quad;
+      float sv[16];
+#pragma unroll
+      for (int x = 0; x < 16; ++x) sv[x] = srow[c0 + x];
+      const float sl2 = srow[max(c0 - 2, 0)], sl1 = srow[max(c0 - 1, 0)];
+      const float slast = srow[BK - 1];
+      if (j0 == 0 && quad == 0) sFirst[r] = sv[0];
+      if (row_ok && i >= j0 + c0 && i < j0 + c0 + 16) sDiag[r] = srow[i - j0];
+      __syncwarp();   // the row's four lanes have read their scores; P overwrites them
+
       float tmax = -INFINITY;
 #pragma unroll
       for (int x = 0; x < 16; ++x)
-        if (c0 + x < nvis) tmax = fmaxf(tmax, srow[c0 + x]);
+        if (c0 + x < nvis) tmax = fmaxf(tmax, sv[x]);
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
       const float m_new = fmaxf(m_run, tmax);
       const float alpha = (m_new == -INFINITY) ? 1.f : exp_rel(m_run - m_new);
       m_run = m_new;
-#pragma unroll
-      for (int x = 0; x < DQ; ++x) acc[x] *= alpha;
       z_part *= alpha;
       bpend *= alpha;
+      if (quad == 0) sAlpha[r] = alpha;
 
       // left endpoint of segment j0+c0: key j0+c0-1
       float sa, ea, bprev;
@@ -154,22 +257,21 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
         bprev = bpend;
       } else {
         // recompute segment j0+c0-1 (owned by the previous quad) for its right share
-        const float s2 = srow[c0 - 2], s1 = srow[c0 - 1];
         const bool ok = (c0 - 1) < nvis;
-        const float e2 = ok ? exp_rel(s2 - m_new) : 0.f;
-        const float e1 = ok ? exp_rel(s1 - m_new) : 0.f;
+        const float e2 = ok ? exp_rel(sl2 - m_new) : 0.f;
+        const float e1 = ok ? exp_rel(sl1 - m_new) : 0.f;
         float M0, M1;
-        seg_moments01(e2, e1, s1 - s2, M0, M1);
+        seg_moments01(e2, e1, sl1 - sl2, M0, M1);
         bprev = ok ? M1 : 0.f;
-        sa = s1;
+        sa = sl1;
         ea = e1;
       }
-#pragma unroll 4
+#pragma unroll
       for (int x = 0; x < 16; ++x) {
         const int c = c0 + x;
         const bool vis = c < nvis;
         const bool seg_ok = vis && (j0 + c) >= 1;
-        const float sb = srow[c];
+        const float sb = sv[x];
         const float eb = vis ? exp_rel(sb - m_new) : 0.f;
         float A = 0.f, Bv = 0.f;
         if (seg_ok) {
@@ -179,50 +281,84 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
           Bv = M1;
           z_part += M0;
         }
-        Ps[r * L::PLD + c] = bprev + A;
+        srow[c] = bprev + A;
         bprev = Bv;
         sa = sb;
         ea = eb;
       }
-      if (j0 == 0 && quad == 0) sFirst[r] = srow[0];
-      if (row_ok && i >= j0 + c0 && i < j0 + c0 + 16) sDiag[r] = srow[i - j0];
       bpend = __shfl_sync(0xffffffffu, bprev, (lane & ~3) | 3);
-      sprev = srow[BK - 1];
+      sprev = slast;
     }
     __syncthreads();
-    // O += P V  (thread: row r, columns d = quad + 4x)
-    for (int c = 0; c < BK; ++c) {
-      const float p = Ps[r * L::PLD + c];
-      const float* vrow = Vs + c * DP + quad;
+    // O = alpha O + P V'  (rows 4ty+a, columns tx*CW ..)
+    {
 #pragma unroll
-      for (int x = 0; x < DQ; ++x) acc[x] = fmaf(p, vrow[4 * x], acc[x]);
+      for (int a = 0; a < 4; ++a) {
+        const float al = sAlpha[4 * ty + a];
+#pragma unroll
+        for (int w = 0; w < CW; ++w) acc[a][w] *= al;
+      }
+#pragma unroll 2
+      for (int c = 0; c < BK; c += 4) {
+        float4 pa[4];
+        float vb[4][CW];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) pa[a] = *reinterpret_cast<const float4*>(Ss + (4 * ty + a) * SLD + c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) lds_cols<CW>(vb[u], Vs + (c + u) * LD + tx * CW);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int w = 0; w < CW; ++w) {
+            float y = fmaf(pa[a].x, vb[0][w], acc[a][w]);
+            y = fmaf(pa[a].y, vb[1][w], y);
+            y = fmaf(pa[a].z, vb[2][w], y);
+            acc[a][w] = fmaf(pa[a].w, vb[3][w], y);
+          }
+      }
     }
   }
 
   // epilogue: caps, last pending weight, normalisation
   z_part += __shfl_xor_sync(0xffffffffu, z_part, 1);
   z_part += __shfl_xor_sync(0xffffffffu, z_part, 2);
-  if (!row_ok) return;
-  const float e0 = exp_rel(sFirst[r] - m_run);
-  const float ei = exp_rel(sDiag[r] - m_run);
-  const float Z = z_part + 0.5f * e0 + 0.5f * ei;
-  const float w0 = 0.5f * e0, wi = bpend + 0.5f * ei;
-  const float inv = 1.f / Z;
-  const T* v0 = v + base;
-  const T* vi = v + base + (size_t)i * D;
-  T* orow = o + act_row((size_t)bh * Tn + i, Tn, H, o_bthd) * D;
-#pragma unroll
-  for (int x = 0; x < DQ; ++x) {
-    const int d = quad + 4 * x;
-    if (d < D) {
-      const float y = (acc[x] + w0 * to_f32(v0[d]) + wi * to_f32(vi[d])) * inv;
-      orow[d] = from_f32<T>(y);
-      if (o32) o32[base + (size_t)i * D + d] = y;
+  if (quad == 0) {
+    float w0 = 0.f, wi = 0.f, inv = 0.f;
+    if (row_ok) {
+      const float e0 = exp_rel(sFirst[r] - m_run);
+      const float ei = exp_rel(sDiag[r] - m_run);
+      const float Z = z_part + 0.5f * e0 + 0.5f * ei;
+      w0 = 0.5f * e0;
+      wi = bpend + 0.5f * ei;
+      inv = 1.f / Z;
+      if (stats) {   // stats == nullptr: inference, no backward follows
+        stats[2 * ((size_t)bh * Tn + i)] = m_run;
+        stats[2 * ((size_t)bh * Tn + i) + 1] = Z;
+      }
     }
+    sW0[r] = w0;
+    sWi[r] = wi;
+    sInv[r] = inv;
   }
-  if (quad == 0 && stats) {   // stats == nullptr: inference, no backward follows
-    stats[2 * ((size_t)bh * Tn + i)] = m_run;
-    stats[2 * ((size_t)bh * Tn + i) + 1] = Z;
+  __syncthreads();
+  const int col0 = tx * CW;
+  float v0[CW];
+#pragma unroll
+  for (int w = 0; w < CW; ++w) v0[w] = (col0 + w < D) ? to_f32(v[base + col0 + w]) : 0.f;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int rr = 4 * ty + a, row = q0 + rr;
+    if (row >= Tn) continue;
+    const float w0 = sW0[rr], wi = sWi[rr], inv = sInv[rr];
+    const T* vi = v + base + (size_t)row * D;
+    float y[CW];
+#pragma unroll
+    for (int w = 0; w < CW; ++w) {
+      const float vv = (col0 + w < D) ? to_f32(vi[col0 + w]) : 0.f;
+      y[w] = (acc[a][w] + w0 * v0[w] + wi * vv) * inv;
+    }
+    store_cols<T, CW>(o + act_row((size_t)bh * Tn + row, Tn, H, o_bthd) * D, col0, y, D, vec);
+    if (o32) store_cols<float, CW>(o32 + base + (size_t)row * D, col0, y, D, vec);
   }
 }
 
@@ -231,19 +367,16 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 
 template <int DP>
 struct BwdSmem {
-  static constexpr int LD = DP + 1;
+  static constexpr int LD = DP + 4;
   static constexpr int HK = BK + 2;      // keys j0-1 .. j0+64
-  static constexpr int SLD = BK + 3;     // score / dP row over the HK keys (padded)
-  static constexpr int PLD = BK + 1;
+  static constexpr int SLD = BK + 4;     // S / dP row over the HK keys, then P / scale*dS in place
   static constexpr int kK = 0;
   static constexpr int kV = kK + HK * LD;
   static constexpr int kQ = kV + HK * LD;
   static constexpr int kO = kQ + BQ * LD;
   static constexpr int kS = kO + BQ * LD;
   static constexpr int kDP = kS + BQ * SLD;
-  static constexpr int kP = kDP + BQ * SLD;
-  static constexpr int kDS = kP + BQ * PLD;
-  static constexpr int kM = kDS + BQ * PLD;
+  static constexpr int kM = kDP + BQ * SLD;
   static constexpr int kIZ = kM + BQ;
   static constexpr int kDD = kIZ + BQ;
   static constexpr int kRed = kDD + BQ;
@@ -252,25 +385,24 @@ struct BwdSmem {
 };
 
 template <typename T, int DP>
-__global__ void __launch_bounds__(NT)
+__global__ void __launch_bounds__(NT, DP <= 64 ? 2 : 1)
 bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ dout, const float* __restrict__ log_gain,
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            float* __restrict__ dq_acc, T* __restrict__ dk, T* __restrict__ dv,
-           float* __restrict__ gain_part, int BH, int H, int Tn, int D, float inv_sqrt_d, int do_bthd) {
+           float* __restrict__ gain_part, int BH, int H, int Tn, int D, float inv_sqrt_d, int do_bthd, int vec) {
   pdl_wait();
   pdl_launch_dependents();
   using L = BwdSmem<DP>;
-  constexpr int DQ = DP / 4;
-  extern __shared__ float smem[];
+  constexpr int LD = L::LD, SLD = L::SLD, HK = L::HK;
+  constexpr int CW = DP / 16;
+  extern __shared__ __align__(16) float smem[];
   float* Ks = smem + L::kK;
   float* Vs = smem + L::kV;
   float* Qs = smem + L::kQ;
   float* Os = smem + L::kO;    // dO tile
   float* Ss = smem + L::kS;
   float* DPs = smem + L::kDP;
-  float* Ps = smem + L::kP;
-  float* DSs = smem + L::kDS;
   float* sM = smem + L::kM;
   float* sIZ = smem + L::kIZ;
   float* sDD = smem + L::kDD;
@@ -283,32 +415,29 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const int h = bh % H;
   const int j0 = kt * BK;
   const size_t base = (size_t)bh * Tn * D;
+  // dO row t of this head: [B,H,T,D] or [B,T,H,D]
+  const size_t do_off = do_bthd ? ((size_t)(bh / H) * Tn * H + h) * D : base;
+  const size_t do_rs = do_bthd ? (size_t)H * D : (size_t)D;
   const float scale = expf(log_gain[h]) * inv_sqrt_d;
 
   // stationary K and V with one halo key on each side (keys j0-1 .. j0+64)
-  for (int idx = tid; idx < L::HK * DP; idx += NT) {
-    const int c = idx / DP, d = idx % DP, key = j0 - 1 + c;
-    const bool ok = key >= 0 && key < Tn && d < D;
-    Ks[c * L::LD + d] = ok ? to_f32(k[base + (size_t)key * D + d]) : 0.f;
-    Vs[c * L::LD + d] = ok ? to_f32(v[base + (size_t)key * D + d]) : 0.f;
-  }
+  load_tile<T, DP>(Ks, k, base, D, j0 - 1, HK, Tn, D, vec);
+  load_tile<T, DP>(Vs, v, base, D, j0 - 1, HK, Tn, D, vec);
 
-  const int r = tid >> 2, quad = tid & 3;      // row phase: query row r, keys 16*quad..+15
-  const int kc = tid >> 2;                      // dK/dV phase: key kc, columns quad + 4x
-  float dk_acc[DQ], dv_acc[DQ];
+  const int r = tid >> 2, quad = tid & 3;     // row phase: query row r, keys 16*quad .. +15
+  const int ty = tid >> 4, tx = tid & 15;     // S/dP: rows 4ty.., keys tx+16b; dQ: rows 4ty.., columns tx*CW..
+  const int kg = tid & 15, cg = tid >> 4;     // dK/dV: keys 4kg .. 4kg+3, columns cg*CW ..
+  float dk_acc[4][CW], dv_acc[4][CW];
 #pragma unroll
-  for (int x = 0; x < DQ; ++x) dk_acc[x] = dv_acc[x] = 0.f;
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int w = 0; w < CW; ++w) dk_acc[u][w] = dv_acc[u][w] = 0.f;
   float gsum = 0.f;
-  const int ty = tid >> 4, tx = tid & 15;
 
   for (int q0 = j0 - (j0 % BQ); q0 < Tn; q0 += BQ) {
     __syncthreads();
-    for (int idx = tid; idx < BQ * DP; idx += NT) {
-      const int rr = idx / DP, d = idx % DP, row = q0 + rr;
-      const bool ok = row < Tn && d < D;
-      Qs[rr * L::LD + d] = ok ? to_f32(q[base + (size_t)row * D + d]) : 0.f;
-      Os[rr * L::LD + d] = ok ? to_f32(dout[act_row((size_t)bh * Tn + row, Tn, H, do_bthd) * D + d]) : 0.f;
-    }
+    load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
+    load_tile<T, DP>(Os, dout, do_off, do_rs, q0, BQ, Tn, D, vec);
     if (tid < BQ) {
       const int row = q0 + tid;
       if (row < Tn) {
@@ -323,68 +452,89 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       }
     }
     __syncthreads();
-    // S and dP over the 66 keys of the tile + halo: rows ty+16a, halo-key columns tx+16b (b<5)
-    {
-      float sacc[4][5], pacc[4][5];
+    // S (scaled) and dP: keys j0 .. j0+63 (halo index 1 .. 64) as 4x4 register tiles
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const float* A = pass ? Os : Qs;
+      const float* Bm = pass ? Vs : Ks;
+      float sacc[4][4];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 5; ++b) sacc[a][b] = pacc[a][b] = 0.f;
+        for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
 #pragma unroll 2
-      for (int d = 0; d < DP; ++d) {
-        float qa[4], oa[4], kb[5], vb[5];
+      for (int d = 0; d < DP; d += 4) {
+        float4 qa[4], kb[4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          qa[a] = Qs[(ty + 16 * a) * L::LD + d];
-          oa[a] = Os[(ty + 16 * a) * L::LD + d];
-        }
+        for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(A + (4 * ty + a) * LD + d);
 #pragma unroll
-        for (int b = 0; b < 5; ++b) {
-          const int c = min(tx + 16 * b, L::HK - 1);
-          kb[b] = Ks[c * L::LD + d];
-          vb[b] = Vs[c * L::LD + d];
-        }
+        for (int b = 0; b < 4; ++b) kb[b] = *reinterpret_cast<const float4*>(Bm + (1 + tx + 16 * b) * LD + d);
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int b = 0; b < 5; ++b) {
-            sacc[a][b] = fmaf(qa[a], kb[b], sacc[a][b]);
-            pacc[a][b] = fmaf(oa[a], vb[b], pacc[a][b]);
+          for (int b = 0; b < 4; ++b) {
+            float s = fmaf(qa[a].x, kb[b].x, sacc[a][b]);
+            s = fmaf(qa[a].y, kb[b].y, s);
+            s = fmaf(qa[a].z, kb[b].z, s);
+            sacc[a][b] = fmaf(qa[a].w, kb[b].w, s);
           }
       }
+      float* dst = pass ? DPs : Ss;
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 5; ++b) {
-          const int c = tx + 16 * b;
-          if (c < L::HK) {
-            Ss[(ty + 16 * a) * L::SLD + c] = sacc[a][b] * scale;
-            DPs[(ty + 16 * a) * L::SLD + c] = pacc[a][b];
-          }
-        }
+        for (int b = 0; b < 4; ++b) dst[(4 * ty + a) * SLD + 1 + tx + 16 * b] = pass ? sacc[a][b] : sacc[a][b] * scale;
+    }
+    // the halo keys j0-1 and j0+64 (index 0 and HK-1): one dot product per thread
+    {
+      const int hr = tid & 63;
+      const int hx = (tid & 64) ? HK - 1 : 0;
+      const bool dpm = tid >= 128;
+      const float* arow = (dpm ? Os : Qs) + hr * LD;
+      const float* brow = (dpm ? Vs : Ks) + hx * LD;
+      float s = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < DP; d += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(arow + d);
+        const float4 b4 = *reinterpret_cast<const float4*>(brow + d);
+        s = fmaf(a4.x, b4.x, s);
+        s = fmaf(a4.y, b4.y, s);
+        s = fmaf(a4.z, b4.z, s);
+        s = fmaf(a4.w, b4.w, s);
+      }
+      if (dpm)
+        DPs[hr * SLD + hx] = s;
+      else
+        Ss[hr * SLD + hx] = s * scale;
     }
     __syncthreads();
     {
-      // srow[x] / prow[x] hold key j0-1+x
-      const float* srow = Ss + r * L::SLD;
-      const float* prow = DPs + r * L::SLD;
+      // sv[y] / pv[y] hold key j0-1+c0+y (halo index c0+y)
+      float* srow = Ss + r * SLD;
+      float* prow = DPs + r * SLD;
       const int i = q0 + r;
       const bool row_ok = i < Tn;
       const float m = sM[r], iz = sIZ[r], dd = sDD[r];
       const int c0 = 16 * quad;
-      // key j visible iff j <= i; x = j - (j0-1)
+      float sv[18], pv[18];
+#pragma unroll
+      for (int y = 0; y < 18; ++y) {
+        sv[y] = srow[c0 + y];
+        pv[y] = prow[c0 + y];
+      }
+      __syncwarp();   // the row's four lanes have read S / dP; P / dS overwrite them
+      // key j0-1+x visible iff it is >= 0 and <= i
       auto vis = [&](int x) { return row_ok && (j0 - 1 + x) >= 0 && (j0 - 1 + x) <= i; };
-      // segment into key x (left key x-1) is valid iff key x visible and key x >= 1
-      float sa = srow[c0];                    // key j0+c0-1
+      float sa = sv[0];                       // key j0+c0-1
       float ea = vis(c0) ? exp_rel(sa - m) : 0.f;
-      float ga = prow[c0] - dd;
+      float ga = pv[0] - dd;
       float Rprev = 0.f, Bprev = 0.f;          // right shares of the segment into the current key
       {
         const int x = c0 + 1;                  // key j0+c0
-        const float sb = srow[x];
+        const float sb = sv[1];
         const bool ok = vis(x) && (j0 - 1 + x) >= 1;
         const float eb = vis(x) ? exp_rel(sb - m) : 0.f;
-        const float gb = prow[x] - dd;
+        const float gb = pv[1] - dd;
         if (ok) {
           float M0, M1, M2;
           seg_moments012(ea, eb, sb - sa, M0, M1, M2);
@@ -394,15 +544,15 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
         }
         sa = sb; ea = eb; ga = gb;
       }
-#pragma unroll 2
+#pragma unroll
       for (int xx = 0; xx < 16; ++xx) {
         const int x = c0 + 1 + xx;             // current key (halo index)
         const int key = j0 - 1 + x;
         // segment from key x to key x+1
-        const float sb = srow[x + 1];
+        const float sb = sv[xx + 2];
         const bool okn = vis(x + 1);           // right key visible (and >= 1 automatically)
         const float eb = okn ? exp_rel(sb - m) : 0.f;
-        const float gb = prow[x + 1] - dd;
+        const float gb = pv[xx + 2] - dd;
         float Lnext = 0.f, Anext = 0.f, Rn = 0.f, Bn = 0.f;
         if (okn) {
           float M0, M1, M2;
@@ -421,56 +571,91 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
           p = (Bprev + Anext + cap) * iz;
           gsum = fmaf(ds, sa, gsum);
         }
-        DSs[r * L::PLD + x - 1] = ds * scale;
-        Ps[r * L::PLD + x - 1] = p;
+        prow[x - 1] = ds * scale;
+        srow[x - 1] = p;
         Rprev = Rn; Bprev = Bn;
         sa = sb; ea = eb; ga = gb;
       }
     }
     __syncthreads();
-    // dV += P^T dO, dK += (scale dS)^T Q  (thread: key kc, columns quad + 4x)
-    for (int rr = 0; rr < BQ; ++rr) {
-      const float p = Ps[rr * L::PLD + kc];
-      const float g = DSs[rr * L::PLD + kc];
-      const float* orow = Os + rr * L::LD + quad;
-      const float* qrow = Qs + rr * L::LD + quad;
+    // dV += P^T dO, dK += (scale dS)^T Q  (keys 4kg+u, columns cg*CW ..)
+    {
+      const int cc = cg * CW;
+#pragma unroll 2
+      for (int rr = 0; rr < BQ; ++rr) {
+        const float4 p4 = *reinterpret_cast<const float4*>(Ss + rr * SLD + 4 * kg);
+        const float4 g4 = *reinterpret_cast<const float4*>(DPs + rr * SLD + 4 * kg);
+        float ov[CW], qv[CW];
+        lds_cols<CW>(ov, Os + rr * LD + cc);
+        lds_cols<CW>(qv, Qs + rr * LD + cc);
+        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+        const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-      for (int x = 0; x < DQ; ++x) {
-        dv_acc[x] = fmaf(p, orow[4 * x], dv_acc[x]);
-        dk_acc[x] = fmaf(g, qrow[4 * x], dk_acc[x]);
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int w = 0; w < CW; ++w) {
+            dv_acc[u][w] = fmaf(pp[u], ov[w], dv_acc[u][w]);
+            dk_acc[u][w] = fmaf(gg[u], qv[w], dk_acc[u][w]);
+          }
       }
     }
-    // dQ += (scale dS) K  (thread: row r, columns quad + 4x), fp32 atomics
+    // dQ += (scale dS) K  (rows 4ty+a, columns tx*CW ..), fp32 atomics
     {
-      float dqa[DQ];
+      float dqa[4][CW];
 #pragma unroll
-      for (int x = 0; x < DQ; ++x) dqa[x] = 0.f;
-      for (int c = 0; c < BK; ++c) {
-        const float g = DSs[r * L::PLD + c];
-        const float* krow = Ks + (c + 1) * L::LD + quad;
+      for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int x = 0; x < DQ; ++x) dqa[x] = fmaf(g, krow[4 * x], dqa[x]);
+        for (int w = 0; w < CW; ++w) dqa[a][w] = 0.f;
+#pragma unroll 2
+      for (int c = 0; c < BK; c += 4) {
+        float4 g4[4];
+        float kk[4][CW];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) g4[a] = *reinterpret_cast<const float4*>(DPs + (4 * ty + a) * SLD + c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) lds_cols<CW>(kk[u], Ks + (c + 1 + u) * LD + tx * CW);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int w = 0; w < CW; ++w) {
+            float y = fmaf(g4[a].x, kk[0][w], dqa[a][w]);
+            y = fmaf(g4[a].y, kk[1][w], y);
+            y = fmaf(g4[a].z, kk[2][w], y);
+            dqa[a][w] = fmaf(g4[a].w, kk[3][w], y);
+          }
       }
-      const int row = q0 + r;
-      if (row < Tn) {
-        float* dst = dq_acc + base + (size_t)row * D;
+      const int col0 = tx * CW;
 #pragma unroll
-        for (int x = 0; x < DQ; ++x) {
-          const int d = quad + 4 * x;
-          if (d < D) atomicAdd(dst + d, dqa[x]);
+      for (int a = 0; a < 4; ++a) {
+        const int row = q0 + 4 * ty + a;
+        if (row >= Tn) continue;
+        float* dst = dq_acc + base + (size_t)row * D + col0;
+        if (vec) {
+          if constexpr (CW % 4 == 0) {
+#pragma unroll
+            for (int w = 0; w < CW; w += 4)
+              atomicAdd(reinterpret_cast<float4*>(dst + w),
+                        make_float4(dqa[a][w], dqa[a][w + 1], dqa[a][w + 2], dqa[a][w + 3]));
+          } else {
+            atomicAdd(reinterpret_cast<float2*>(dst), make_float2(dqa[a][0], dqa[a][1]));
+          }
+        } else {
+#pragma unroll
+          for (int w = 0; w < CW; ++w)
+            if (col0 + w < D) atomicAdd(dst + w, dqa[a][w]);
         }
       }
     }
   }
 
-  const int key = j0 + kc;
-  if (key < Tn) {
+  {
+    const int cc = cg * CW;
 #pragma unroll
-    for (int x = 0; x < DQ; ++x) {
-      const int d = quad + 4 * x;
-      if (d < D) {
-        dk[base + (size_t)key * D + d] = from_f32<T>(dk_acc[x]);
-        dv[base + (size_t)key * D + d] = from_f32<T>(dv_acc[x]);
+    for (int u = 0; u < 4; ++u) {
+      const int key = j0 + 4 * kg + u;
+      if (key < Tn) {
+        store_cols<T, CW>(dk + base + (size_t)key * D, cc, dk_acc[u], D, vec);
+        store_cols<T, CW>(dv + base + (size_t)key * D, cc, dv_acc[u], D, vec);
       }
     }
   }
@@ -604,6 +789,12 @@ __global__ void cast_gain_kernel(const float* __restrict__ src, T* __restrict__ 
 // ---------------------------------------------------------------------------
 // launchers
 
+// 4-element chunks of T at p are aligned for the vector loads and stores (null passes)
+template <typename T>
+static bool vec_ok(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & (4 * sizeof(T) - 1)) == 0;
+}
+
 template <typename T, int DP>
 static cudaError_t launch_fwd(const FwdArgs& a) {
   auto kern = fwd_kernel<T, DP>;
@@ -612,9 +803,11 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   if (e != cudaSuccess) return e;
   const long long BH = a.B * a.H;
   const long long nqt = (a.T + BQ - 1) / BQ;
+  const int vec = a.D == DP && vec_ok<T>(a.q) && vec_ok<T>(a.k) && vec_ok<T>(a.v) && vec_ok<T>(a.o) &&
+                  vec_ok<float>(a.o_f32);
   return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
                     (const T*)a.v, a.log_gain, (T*)a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T,
-                    (int)a.D, a.inv_sqrt_d, a.o_bthd);
+                    (int)a.D, a.inv_sqrt_d, a.o_bthd, vec);
 }
 
 template <typename T>
@@ -640,10 +833,12 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   if (e != cudaSuccess) return e;
   const long long BH = a.B * a.H;
   const long long nkt = (a.T + BK - 1) / BK;
+  const int vec = a.D == DP && vec_ok<T>(a.q) && vec_ok<T>(a.k) && vec_ok<T>(a.v) && vec_ok<T>(a.d_o) &&
+                  vec_ok<T>(a.dk) && vec_ok<T>(a.dv) && vec_ok<float>(w.dq_acc);
   return launch_pdl(kern, dim3((unsigned)(BH * nkt)), dim3(NT), smem, a.stream, (const T*)a.q, (const T*)a.k,
                     (const T*)a.v, (const T*)a.d_o, a.log_gain, a.row_stats, (const float*)w.rowdot, w.dq_acc,
                     (T*)a.dk, (T*)a.dv, a.dlog_gain ? w.gain_part : nullptr, (int)BH, (int)a.H, (int)a.T,
-                    (int)a.D, a.inv_sqrt_d, a.act_bthd);
+                    (int)a.D, a.inv_sqrt_d, a.act_bthd, vec);
 }
 
 template <typename T>
