@@ -93,20 +93,56 @@ __device__ __forceinline__ void load_tile(float* dst, const T* __restrict__ src,
   }
 }
 
-// CW consecutive floats of a shared row (16-byte aligned for CW % 4 == 0, 8-byte for CW == 2)
+// 16-byte global -> shared copy that bypasses registers (cp.async, L2 only);
+// valid == false writes 16 zero bytes and reads nothing.
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// load_tile for fp32 with D == DP, issued as cp.async copies: the caller commits,
+// waits (cp_async_wait_all) and then synchronises the CTA before reading.
+template <int DP>
+__device__ __forceinline__ void cp_async_tile(float* dst, const float* __restrict__ src, size_t off, size_t rs,
+                                              int row0, int n, int Tn) {
+  constexpr int LD = DP + 4, C4 = DP / 4;
+  for (int idx = threadIdx.x; idx < n * C4; idx += NT) {
+    const int rr = idx / C4, c = (idx - rr * C4) * 4, row = row0 + rr;
+    const bool ok = row >= 0 && row < Tn;
+    cp_async16(dst + rr * LD + c, ok ? src + off + (size_t)row * rs + c : src, ok);
+  }
+}
+
+// CW consecutive floats of a shared row as CW/2 register pairs
 template <int CW>
-__device__ __forceinline__ void lds_cols(float (&dst)[CW], const float* p) {
+__device__ __forceinline__ void lds_pairs(float2 (&dst)[CW / 2], const float* p) {
   if constexpr (CW % 4 == 0) {
 #pragma unroll
     for (int w = 0; w < CW; w += 4) {
       const float4 x = *reinterpret_cast<const float4*>(p + w);
-      dst[w] = x.x; dst[w + 1] = x.y; dst[w + 2] = x.z; dst[w + 3] = x.w;
+      dst[w / 2] = make_float2(x.x, x.y);
+      dst[w / 2 + 1] = make_float2(x.z, x.w);
     }
   } else {
     static_assert(CW == 2, "DP must be 32, 64 or 128");
-    const float2 x = *reinterpret_cast<const float2*>(p);
-    dst[0] = x.x; dst[1] = x.y;
+    dst[0] = *reinterpret_cast<const float2*>(p);
   }
+}
+
+// S += A B^T over 4 reduction indices for a 4x4 tile, in packed pairs: lane x of
+// acc[a][b] sums the even reduction indices, lane y the odd ones (the tile's
+// result is x + y).
+__device__ __forceinline__ void tile4x4_pairs(float2 (&acc)[4][4], const float4 (&qa)[4], const float4 (&kb)[4]) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      acc[a][b] = fma2(make_float2(qa[a].x, qa[a].y), make_float2(kb[b].x, kb[b].y), acc[a][b]);
+      acc[a][b] = fma2(make_float2(qa[a].z, qa[a].w), make_float2(kb[b].z, kb[b].w), acc[a][b]);
+    }
 }
 
 // CW consecutive outputs of one row: columns col0 .. col0+CW-1 of a D-wide row
@@ -130,16 +166,16 @@ struct FwdSmem {
   static constexpr int LD = DP + 4;      // Q / K / V' rows
   static constexpr int SLD = BK + 4;     // score row (keys j0 .. j0+63), then its P row in place
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + BQ * LD;
-  static constexpr int kV = kK + BK * LD;
-  static constexpr int kS = kV + BK * LD;
+  static constexpr int kK = kQ + BQ * LD;     // two K buffers (key tile kt in buffer kt & 1)
+  static constexpr int kV = kK + 2 * BK * LD; // two V' buffers
+  static constexpr int kS = kV + 2 * BK * LD;
   static constexpr int kRow = kS + BQ * SLD;   // per-row alpha, first, diag, w0, wi, 1/Z
   static constexpr int kFloats = kRow + 6 * BQ;
   static constexpr size_t bytes = sizeof(float) * kFloats;
 };
 
 template <typename T, int DP>
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NT, DP <= 64 ? 2 : 1)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const float* __restrict__ log_gain, T* __restrict__ o, float* __restrict__ o32,
            float* __restrict__ stats, int BH, int H, int Tn, int D, float inv_sqrt_d, int o_bthd, int vec) {
@@ -169,7 +205,18 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const size_t base = (size_t)bh * Tn * D;
   const float scale = expf(log_gain[h]) * inv_sqrt_d;
 
-  load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
+  // fp32 tiles stream in by cp.async: key tile kt+1 is copied while tile kt is
+  // computed; other element types convert through registers, tile by tile.
+  const bool async = sizeof(T) == 4 && vec;
+  if (async) {
+    const float* qf = reinterpret_cast<const float*>(q);
+    cp_async_tile<DP>(Qs, qf, base, D, q0, BQ, Tn);
+    cp_async_tile<DP>(Ks, reinterpret_cast<const float*>(k), base, D, 0, BK, Tn);
+    cp_async_tile<DP>(Vs, reinterpret_cast<const float*>(v), base, D, -1, BK, Tn);
+    cp_async_commit();
+  } else {
+    load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
+  }
 
   // row phase: 4 consecutive lanes share query row r, keys 16*quad .. +15
   const int r = tid >> 2, quad = tid & 3;
@@ -179,48 +226,54 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   float m_run = -INFINITY, z_part = 0.f, bpend = 0.f, sprev = 0.f;
   // tile phases: rows 4ty .. 4ty+3; keys tx + 16b (S) or O columns tx*CW .. (P V')
   const int ty = tid >> 4, tx = tid & 15;
-  float acc[4][CW];
+  constexpr int CP = CW / 2;             // O column pairs per thread
+  float2 acc[4][CP];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int w = 0; w < CW; ++w) acc[a][w] = 0.f;
+    for (int w = 0; w < CP; ++w) acc[a][w] = make_float2(0.f, 0.f);
 
   const int last_row = min(q0 + BQ, Tn) - 1;
   const int nkt = last_row / BK + 1;
 
   for (int kt = 0; kt < nkt; ++kt) {
     const int j0 = kt * BK;
-    __syncthreads();
-    load_tile<T, DP>(Ks, k, base, D, j0, BK, Tn, D, vec);
-    load_tile<T, DP>(Vs, v, base, D, j0 - 1, BK, Tn, D, vec);   // V' row c = key j0-1+c
-    __syncthreads();
+    float* Kb = Ks + (kt & 1) * BK * LD;
+    float* Vb = Vs + (kt & 1) * BK * LD;     // V' row c = key j0-1+c
+    if (async) {
+      cp_async_wait_all();
+      __syncthreads();   // tile kt visible; every thread is past tile kt-1, whose buffers refill now
+      if (kt + 1 < nkt) {
+        const int nb = ((kt + 1) & 1) * BK * LD;
+        cp_async_tile<DP>(Ks + nb, reinterpret_cast<const float*>(k), base, D, j0 + BK, BK, Tn);
+        cp_async_tile<DP>(Vs + nb, reinterpret_cast<const float*>(v), base, D, j0 + BK - 1, BK, Tn);
+        cp_async_commit();
+      }
+    } else {
+      __syncthreads();
+      load_tile<T, DP>(Kb, k, base, D, j0, BK, Tn, D, vec);
+      load_tile<T, DP>(Vb, v, base, D, j0 - 1, BK, Tn, D, vec);
+      __syncthreads();
+    }
     {
-      float sacc[4][4];
+      float2 sacc[4][4];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
+        for (int b = 0; b < 4; ++b) sacc[a][b] = make_float2(0.f, 0.f);
 #pragma unroll 2
       for (int d = 0; d < DP; d += 4) {
         float4 qa[4], kb[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(Qs + (4 * ty + a) * LD + d);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) kb[b] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * b) * LD + d);
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            float s = fmaf(qa[a].x, kb[b].x, sacc[a][b]);
-            s = fmaf(qa[a].y, kb[b].y, s);
-            s = fmaf(qa[a].z, kb[b].z, s);
-            sacc[a][b] = fmaf(qa[a].w, kb[b].w, s);
-          }
+        for (int b = 0; b < 4; ++b) kb[b] = *reinterpret_cast<const float4*>(Kb + (tx + 16 * b) * LD + d);
+        tile4x4_pairs(sacc, qa, kb);
       }
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) Ss[(4 * ty + a) * SLD + tx + 16 * b] = sacc[a][b] * scale;
+        for (int b = 0; b < 4; ++b) Ss[(4 * ty + a) * SLD + tx + 16 * b] = (sacc[a][b].x + sacc[a][b].y) * scale;
     }
     __syncthreads();
     {
@@ -294,27 +347,28 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     {
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
-        const float al = sAlpha[4 * ty + a];
+        const float2 al = splat2(sAlpha[4 * ty + a]);
 #pragma unroll
-        for (int w = 0; w < CW; ++w) acc[a][w] *= al;
+        for (int w = 0; w < CP; ++w) acc[a][w] = mul2(acc[a][w], al);
       }
 #pragma unroll 2
       for (int c = 0; c < BK; c += 4) {
         float4 pa[4];
-        float vb[4][CW];
+        float2 vb[4][CP];
 #pragma unroll
         for (int a = 0; a < 4; ++a) pa[a] = *reinterpret_cast<const float4*>(Ss + (4 * ty + a) * SLD + c);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) lds_cols<CW>(vb[u], Vs + (c + u) * LD + tx * CW);
+        for (int u = 0; u < 4; ++u) lds_pairs<CW>(vb[u], Vb + (c + u) * LD + tx * CW);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < 4; ++a) {
+          const float pu[4] = {pa[a].x, pa[a].y, pa[a].z, pa[a].w};
 #pragma unroll
-          for (int w = 0; w < CW; ++w) {
-            float y = fmaf(pa[a].x, vb[0][w], acc[a][w]);
-            y = fmaf(pa[a].y, vb[1][w], y);
-            y = fmaf(pa[a].z, vb[2][w], y);
-            acc[a][w] = fmaf(pa[a].w, vb[3][w], y);
+          for (int u = 0; u < 4; ++u) {
+            const float2 pp = splat2(pu[u]);
+#pragma unroll
+            for (int w = 0; w < CP; ++w) acc[a][w] = fma2(pp, vb[u][w], acc[a][w]);
           }
+        }
       }
     }
   }
@@ -355,7 +409,8 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 #pragma unroll
     for (int w = 0; w < CW; ++w) {
       const float vv = (col0 + w < D) ? to_f32(vi[col0 + w]) : 0.f;
-      y[w] = (acc[a][w] + w0 * v0[w] + wi * vv) * inv;
+      const float av = (w & 1) ? acc[a][w / 2].y : acc[a][w / 2].x;
+      y[w] = (av + w0 * v0[w] + wi * vv) * inv;
     }
     store_cols<T, CW>(o + act_row((size_t)bh * Tn + row, Tn, H, o_bthd) * D, col0, y, D, vec);
     if (o32) store_cols<float, CW>(o32 + base + (size_t)row * D, col0, y, D, vec);
@@ -427,29 +482,50 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const int r = tid >> 2, quad = tid & 3;     // row phase: query row r, keys 16*quad .. +15
   const int ty = tid >> 4, tx = tid & 15;     // S/dP: rows 4ty.., keys tx+16b; dQ: rows 4ty.., columns tx*CW..
   const int kg = tid & 15, cg = tid >> 4;     // dK/dV: keys 4kg .. 4kg+3, columns cg*CW ..
-  float dk_acc[4][CW], dv_acc[4][CW];
+  constexpr int CP = CW / 2;             // column pairs per thread
+  float2 dk_acc[4][CP], dv_acc[4][CP];
 #pragma unroll
   for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int w = 0; w < CW; ++w) dk_acc[u][w] = dv_acc[u][w] = 0.f;
+    for (int w = 0; w < CP; ++w) dk_acc[u][w] = dv_acc[u][w] = make_float2(0.f, 0.f);
   float gsum = 0.f;
 
-  for (int q0 = j0 - (j0 % BQ); q0 < Tn; q0 += BQ) {
-    __syncthreads();
-    load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
-    load_tile<T, DP>(Os, dout, do_off, do_rs, q0, BQ, Tn, D, vec);
-    if (tid < BQ) {
-      const int row = q0 + tid;
-      if (row < Tn) {
-        const size_t ri = (size_t)bh * Tn + row;
-        sM[tid] = stats[2 * ri];
-        sIZ[tid] = 1.f / stats[2 * ri + 1];
-        sDD[tid] = rowdot[ri];
-      } else {
-        sM[tid] = 0.f;
-        sIZ[tid] = 0.f;
-        sDD[tid] = 0.f;
-      }
+  // fp32 query tiles stream in by cp.async: tile q0+BQ is copied during the dQ
+  // product of tile q0 (which reads only dS and K); other element types convert
+  // through registers, tile by tile.  Threads 0..63 fetch the row statistics of
+  // the next tile into registers ahead of time as well.
+  const bool async = sizeof(T) == 4 && vec;
+  const int qfirst = j0 - (j0 % BQ);
+  auto row_stats = [&](int q0, float& m, float& iz, float& dd) {
+    const int row = q0 + tid;
+    m = 0.f; iz = 0.f; dd = 0.f;
+    if (row < Tn) {
+      const size_t ri = (size_t)bh * Tn + row;
+      m = stats[2 * ri];
+      iz = 1.f / stats[2 * ri + 1];
+      dd = rowdot[ri];
+    }
+  };
+  float nM = 0.f, nIZ = 0.f, nDD = 0.f;
+  if (tid < BQ) row_stats(qfirst, nM, nIZ, nDD);
+  if (async) {
+    cp_async_tile<DP>(Qs, reinterpret_cast<const float*>(q), base, D, qfirst, BQ, Tn);
+    cp_async_tile<DP>(Os, reinterpret_cast<const float*>(dout), do_off, do_rs, qfirst, BQ, Tn);
+    cp_async_commit();
+  }
+
+  for (int q0 = qfirst; q0 < Tn; q0 += BQ) {
+    if (async) {
+      cp_async_wait_all();
+    } else {
+      __syncthreads();
+      load_tile<T, DP>(Qs, q, base, D, q0, BQ, Tn, D, vec);
+      load_tile<T, DP>(Os, dout, do_off, do_rs, q0, BQ, Tn, D, vec);
+    }
+    if (tid < BQ) {   // the previous tile's readers of these passed two barriers since
+      sM[tid] = nM;
+      sIZ[tid] = nIZ;
+      sDD[tid] = nDD;
     }
     __syncthreads();
     // S (scaled) and dP: keys j0 .. j0+63 (halo index 1 .. 64) as 4x4 register tiles
@@ -457,11 +533,11 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     for (int pass = 0; pass < 2; ++pass) {
       const float* A = pass ? Os : Qs;
       const float* Bm = pass ? Vs : Ks;
-      float sacc[4][4];
+      float2 sacc[4][4];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
+        for (int b = 0; b < 4; ++b) sacc[a][b] = make_float2(0.f, 0.f);
 #pragma unroll 2
       for (int d = 0; d < DP; d += 4) {
         float4 qa[4], kb[4];
@@ -469,21 +545,16 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
         for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(A + (4 * ty + a) * LD + d);
 #pragma unroll
         for (int b = 0; b < 4; ++b) kb[b] = *reinterpret_cast<const float4*>(Bm + (1 + tx + 16 * b) * LD + d);
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            float s = fmaf(qa[a].x, kb[b].x, sacc[a][b]);
-            s = fmaf(qa[a].y, kb[b].y, s);
-            s = fmaf(qa[a].z, kb[b].z, s);
-            sacc[a][b] = fmaf(qa[a].w, kb[b].w, s);
-          }
+        tile4x4_pairs(sacc, qa, kb);
       }
       float* dst = pass ? DPs : Ss;
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) dst[(4 * ty + a) * SLD + 1 + tx + 16 * b] = pass ? sacc[a][b] : sacc[a][b] * scale;
+        for (int b = 0; b < 4; ++b) {
+          const float x = sacc[a][b].x + sacc[a][b].y;
+          dst[(4 * ty + a) * SLD + 1 + tx + 16 * b] = pass ? x : x * scale;
+        }
     }
     // the halo keys j0-1 and j0+64 (index 0 and HK-1): one dot product per thread
     {
@@ -492,16 +563,15 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       const bool dpm = tid >= 128;
       const float* arow = (dpm ? Os : Qs) + hr * LD;
       const float* brow = (dpm ? Vs : Ks) + hx * LD;
-      float s = 0.f;
+      float2 s2 = make_float2(0.f, 0.f);   // even / odd d, summed like the tiles
 #pragma unroll 4
       for (int d = 0; d < DP; d += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(arow + d);
         const float4 b4 = *reinterpret_cast<const float4*>(brow + d);
-        s = fmaf(a4.x, b4.x, s);
-        s = fmaf(a4.y, b4.y, s);
-        s = fmaf(a4.z, b4.z, s);
-        s = fmaf(a4.w, b4.w, s);
+        s2 = fma2(make_float2(a4.x, a4.y), make_float2(b4.x, b4.y), s2);
+        s2 = fma2(make_float2(a4.z, a4.w), make_float2(b4.z, b4.w), s2);
       }
+      const float s = s2.x + s2.y;
       if (dpm)
         DPs[hr * SLD + hx] = s;
       else
@@ -585,45 +655,65 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
       for (int rr = 0; rr < BQ; ++rr) {
         const float4 p4 = *reinterpret_cast<const float4*>(Ss + rr * SLD + 4 * kg);
         const float4 g4 = *reinterpret_cast<const float4*>(DPs + rr * SLD + 4 * kg);
-        float ov[CW], qv[CW];
-        lds_cols<CW>(ov, Os + rr * LD + cc);
-        lds_cols<CW>(qv, Qs + rr * LD + cc);
+        float2 ov[CP], qv[CP];
+        lds_pairs<CW>(ov, Os + rr * LD + cc);
+        lds_pairs<CW>(qv, Qs + rr * LD + cc);
         const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
         const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 4; ++u) {
+          const float2 p2 = splat2(pp[u]), g2 = splat2(gg[u]);
 #pragma unroll
-          for (int w = 0; w < CW; ++w) {
-            dv_acc[u][w] = fmaf(pp[u], ov[w], dv_acc[u][w]);
-            dk_acc[u][w] = fmaf(gg[u], qv[w], dk_acc[u][w]);
+          for (int w = 0; w < CP; ++w) {
+            dv_acc[u][w] = fma2(p2, ov[w], dv_acc[u][w]);
+            dk_acc[u][w] = fma2(g2, qv[w], dk_acc[u][w]);
           }
+        }
+      }
+    }
+    if (q0 + BQ < Tn) {
+      if (tid < BQ) row_stats(q0 + BQ, nM, nIZ, nDD);
+      if (async) {
+        __syncthreads();   // every thread is done with this Q / dO tile
+        cp_async_tile<DP>(Qs, reinterpret_cast<const float*>(q), base, D, q0 + BQ, BQ, Tn);
+        cp_async_tile<DP>(Os, reinterpret_cast<const float*>(dout), do_off, do_rs, q0 + BQ, BQ, Tn);
+        cp_async_commit();
       }
     }
     // dQ += (scale dS) K  (rows 4ty+a, columns tx*CW ..), fp32 atomics
     {
+      float2 dq2[4][CP];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int w = 0; w < CP; ++w) dq2[a][w] = make_float2(0.f, 0.f);
+#pragma unroll 2
+      for (int c = 0; c < BK; c += 4) {
+        float4 g4[4];
+        float2 kk[4][CP];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) g4[a] = *reinterpret_cast<const float4*>(DPs + (4 * ty + a) * SLD + c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) lds_pairs<CW>(kk[u], Ks + (c + 1 + u) * LD + tx * CW);
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const float gu[4] = {g4[a].x, g4[a].y, g4[a].z, g4[a].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float2 g2 = splat2(gu[u]);
+#pragma unroll
+            for (int w = 0; w < CP; ++w) dq2[a][w] = fma2(g2, kk[u][w], dq2[a][w]);
+          }
+        }
+      }
       float dqa[4][CW];
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int w = 0; w < CW; ++w) dqa[a][w] = 0.f;
-#pragma unroll 2
-      for (int c = 0; c < BK; c += 4) {
-        float4 g4[4];
-        float kk[4][CW];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) g4[a] = *reinterpret_cast<const float4*>(DPs + (4 * ty + a) * SLD + c);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) lds_cols<CW>(kk[u], Ks + (c + 1 + u) * LD + tx * CW);
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int w = 0; w < CW; ++w) {
-            float y = fmaf(g4[a].x, kk[0][w], dqa[a][w]);
-            y = fmaf(g4[a].y, kk[1][w], y);
-            y = fmaf(g4[a].z, kk[2][w], y);
-            dqa[a][w] = fmaf(g4[a].w, kk[3][w], y);
-          }
-      }
+        for (int w = 0; w < CP; ++w) {
+          dqa[a][2 * w] = dq2[a][w].x;
+          dqa[a][2 * w + 1] = dq2[a][w].y;
+        }
       const int col0 = tx * CW;
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
@@ -654,8 +744,16 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     for (int u = 0; u < 4; ++u) {
       const int key = j0 + 4 * kg + u;
       if (key < Tn) {
-        store_cols<T, CW>(dk + base + (size_t)key * D, cc, dk_acc[u], D, vec);
-        store_cols<T, CW>(dv + base + (size_t)key * D, cc, dv_acc[u], D, vec);
+        float kx[CW], vx[CW];
+#pragma unroll
+        for (int w = 0; w < CP; ++w) {
+          kx[2 * w] = dk_acc[u][w].x;
+          kx[2 * w + 1] = dk_acc[u][w].y;
+          vx[2 * w] = dv_acc[u][w].x;
+          vx[2 * w + 1] = dv_acc[u][w].y;
+        }
+        store_cols<T, CW>(dk + base + (size_t)key * D, cc, kx, D, vec);
+        store_cols<T, CW>(dv + base + (size_t)key * D, cc, vx, D, vec);
       }
     }
   }
