@@ -1,0 +1,135 @@
+"""The operator against the reference's own CUDA kernels on the GPU, and both timed.
+
+The float64 oracle checks the operator at sizes it finishes in seconds.  Here the
+reference's compiled extension (oracle/ref_cuda.py, built from the reference's
+sources into oracle/_ref/) is the second oracle at full size: config 2 in the
+reference's fp16 ``prefix_v6`` mode and its ``prefix`` mode (fp16, bf16, fp32), and
+a long-sequence fp32 case with the config-3 input recipe.  The bar is the one the
+reference applies between its own CUDA modes (cuda/benchmark.py:22-31, 44-50):
+relative L2 error <= 1e-3 for the output and every gradient (1e-4 in fp32), or,
+for 16-bit inputs, no further from the reference's fp32 path than its own 16-bit
+path is.
+
+``test_reference_cuda_timing_config2`` times both at config 2 the way the
+reference's speed phase does (cuda/benchmark.py:111-125: CUDA events around the
+op and around ``autograd.grad`` of ``(y * dy).sum()``, medians over repeats) and
+prints one ``REFERENCE_CUDA_B200`` JSON line.
+
+Skipped when the extension has not been built (it needs the reference project
+at build time).
+"""
+import json
+import statistics
+
+import pytest
+import torch
+
+from oracle import ref_cuda
+import continuum_attention_b200 as ca
+from ca_testlib import gen_inputs
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not ref_cuda.available(), reason="reference CUDA extension not built")]
+
+REL_L2 = 1e-3   # the reference's own bar between its CUDA modes (cuda/benchmark.py --rel-tol)
+
+
+def _rel_l2(a, b):
+    a, b = a.detach().double(), b.detach().double()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def _run(fn, q, k, v, lg, dy):
+    q, k, v, lg = (t.detach().clone().requires_grad_(True) for t in (q, k, v, lg))
+    y = fn(q, k, v, lg)
+    grads = torch.autograd.grad((y.float() * dy.float()).sum(), (q, k, v, lg))
+    return [y] + list(grads)
+
+
+def _ours(q, k, v, lg):
+    return ca.continuum_attention(q, k, v, lg, 128)
+
+
+def _ref(mode):
+    return lambda q, k, v, lg: ref_cuda.ref_continuum_attention(q, k, v, lg, 128, mode)
+
+
+def _config2(dtype, seed=1649):
+    g = torch.Generator().manual_seed(seed)
+    shape = (2, 16, 2048, 64)
+    q, k, v, dy = (torch.randn(shape, generator=g).to("cuda", dtype) for _ in range(4))
+    return q, k, v, torch.zeros(16, device="cuda"), dy
+
+
+@pytest.mark.parametrize("mode,dtype", [("prefix_v6", torch.float16), ("prefix", torch.float16),
+                                        ("prefix", torch.bfloat16), ("prefix", torch.float32)])
+def test_config2_matches_reference_cuda(mode, dtype):
+    """Against the reference's fp32 ``prefix`` path on the same (rounded) inputs.
+
+    fp32: relative L2 <= 1e-4.  fp16 / bf16: within the reference's bar between its
+    modes, or no further from the fp32 path than the reference's own kernels in
+    that mode and dtype are (its bf16 path rounds the weights W to bf16 before
+    W V, which alone costs ~3e-3).
+    """
+    q, k, v, lg, dy = _config2(dtype)
+    ours = _run(_ours, q, k, v, lg, dy)
+    ref = _run(_ref(mode), q, k, v, lg, dy)
+    exact = ref if dtype == torch.float32 else _run(_ref("prefix"), q.float(), k.float(), v.float(), lg,
+                                                    dy.float())
+    torch.cuda.synchronize()
+    names = ("y", "dq", "dk", "dv", "dlog_gain")
+    rec = {"mode": mode, "dtype": str(dtype)}
+    for n, a, b, x in zip(names, ours, ref, exact):
+        e_ours, e_ref = _rel_l2(a, x), _rel_l2(b, x)
+        rec[n] = {"ours": e_ours, "reference": e_ref, "ours_vs_reference": _rel_l2(a, b)}
+        bar = 1e-4 if dtype == torch.float32 else max(REL_L2, 1.05 * e_ref)
+        assert e_ours <= bar, f"{mode} {dtype} {n}: relative L2 {e_ours:.3e} > {bar:.3e}"
+    print("REFERENCE_CUDA_COMPARE", json.dumps(rec), flush=True)
+
+
+def test_long_fp32_matches_reference_prefix():
+    # config-3 recipe (score std ~4, 10% duplicated keys) at T = 4096, fp32
+    q, k, v, dy = (t.cuda() for t in gen_inputs((1, 4, 4096, 64), seed=33, qk_mag=2.0, dup_frac=0.1))
+    lg = torch.tensor([0.0, 0.3, -0.3, 1.0], device="cuda")
+    ours = _run(_ours, q, k, v, lg, dy)
+    ref = _run(_ref("prefix"), q, k, v, lg, dy)
+    torch.cuda.synchronize()
+    errs = {n: _rel_l2(a, b) for n, a, b in zip(("y", "dq", "dk", "dv", "dlog_gain"), ours, ref)}
+    print("REFERENCE_CUDA_COMPARE", json.dumps({"mode": "prefix", "dtype": "fp32 T=4096", **errs}), flush=True)
+    for n, e in errs.items():
+        assert e <= 1e-4, f"{n}: relative L2 {e:.3e} > 1e-4"
+
+
+def _timed(fn, inputs, warmup=2, repeats=7):
+    def step(i):
+        q, k, v, lg, dy = inputs[i % len(inputs)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        y = fn(q, k, v, lg)
+        ev[1].record()
+        torch.autograd.grad((y.float() * dy.float()).sum(), (q, k, v, lg))
+        ev[2].record()
+        return ev
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    evs = [step(i) for i in range(repeats)]
+    torch.cuda.synchronize()
+    med = lambda a, b: statistics.median(e[a].elapsed_time(e[b]) for e in evs)
+    return {"forward_ms": med(0, 1), "backward_ms": med(1, 2), "total_ms": med(0, 2)}
+
+
+def test_reference_cuda_timing_config2():
+    res = {}
+    for name, fn, dtype in (("reference prefix_v6 fp16", _ref("prefix_v6"), torch.float16),
+                            ("reference prefix bf16", _ref("prefix"), torch.bfloat16),
+                            ("ours fp16", _ours, torch.float16),
+                            ("ours bf16", _ours, torch.bfloat16)):
+        sets = []
+        for s in range(2):
+            q, k, v, lg, dy = _config2(dtype, seed=1649 + s)
+            sets.append(tuple(t.requires_grad_(True) for t in (q, k, v, lg)) + (dy,))
+        res[name] = _timed(fn, sets)
+    print("REFERENCE_CUDA_B200", json.dumps({"shape": [2, 16, 2048, 64], "query_tile": 128, **res}), flush=True)
+    assert res["ours fp16"]["total_ms"] < res["reference prefix_v6 fp16"]["total_ms"]
