@@ -44,6 +44,8 @@ SIGNATURES = {
     "ca_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _int, _int, _vp]),
     "ca_add_rmsnorm_forward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "ca_add_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _i64, _vp]),
+    "ca_gelu_tanh_forward": (_int, [_vp, _vp, _i64, _int, _vp]),
+    "ca_gelu_tanh_backward": (_int, [_vp, _vp, _vp, _i64, _int, _vp]),
 }
 
 _lock = threading.Lock()

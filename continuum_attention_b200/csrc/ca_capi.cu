@@ -372,6 +372,40 @@ int ca_selftest_wait_timeout(int64_t limit_us, void* stream) {
   return ok();
 }
 
+static int check_gelu(const char* fn, int64_t n, int dtype, std::initializer_list<const void*> ptrs) {
+  if (dtype < CA_DTYPE_F32 || dtype > CA_DTYPE_F16) return fail(CA_ERR_INVALID_ARGUMENT, "%s: unknown dtype %d", fn, dtype);
+  if (n < 0) return fail(CA_ERR_INVALID_ARGUMENT, "%s: n must be >= 0", fn);
+  const int vec = ca::gelu::vector_elems(dtype);
+  if (n % vec) return fail(CA_ERR_UNSUPPORTED, "%s: n must be a multiple of %d for this dtype", fn, vec);
+  if (n == 0) return CA_OK;
+  for (const void* p : ptrs)
+    if (!p) return fail(CA_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+  if (!all_aligned16(ptrs)) return fail(CA_ERR_INVALID_ARGUMENT, "%s: buffers must be 16-byte aligned", fn);
+  return CA_OK;
+}
+
+int ca_gelu_tanh_forward(const void* x, void* y, int64_t n, int dtype, void* stream) {
+  g_last_launches = 0;
+  int st = check_gelu("ca_gelu_tanh_forward", n, dtype, {x, y});
+  if (st != CA_OK) return st;
+  if (n == 0) return ok();
+  cudaError_t e = ca::gelu::forward(x, y, (size_t)n, dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_gelu_tanh_forward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
+int ca_gelu_tanh_backward(const void* x, const void* dy, void* dx, int64_t n, int dtype, void* stream) {
+  g_last_launches = 0;
+  int st = check_gelu("ca_gelu_tanh_backward", n, dtype, {x, dy, dx});
+  if (st != CA_OK) return st;
+  if (n == 0) return ok();
+  cudaError_t e = ca::gelu::backward(x, dy, dx, (size_t)n, dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "ca_gelu_tanh_backward launch");
+  g_last_launches = 1;
+  return ok();
+}
+
 int ca_device_status(int reset) {
   int value = 0;
   cudaError_t e = ca::read_device_status(&value, reset != 0);

@@ -135,6 +135,14 @@ cudaError_t add_backward(const float* xn, const float* w, const void* dy, const 
                          float* dx, void* dr, float* dw, float* dw_part, long long rows, long long D, cudaStream_t s);
 }  // namespace norm
 
+namespace gelu {
+// tanh-approximate GELU over n contiguous elements (dtype codes as the ABI's);
+// n a multiple of vector_elems(dtype), buffers 16-byte aligned
+int vector_elems(int dtype);
+cudaError_t forward(const void* x, void* y, size_t n, int dtype, cudaStream_t s);
+cudaError_t backward(const void* x, const void* dy, void* dx, size_t n, int dtype, cudaStream_t s);
+}  // namespace gelu
+
 cudaError_t read_device_status(int* out, bool reset);
 
 }  // namespace ca

@@ -25,6 +25,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import continuum_attention
+from .gelu import gelu_tanh
+from .gelu import supported as gelu_supported
 from .rmsnorm import add_rms_norm, add_supported
 from .rmsnorm import rms_norm as native_rms_norm
 from .rmsnorm import supported as native_rms_norm_supported
@@ -120,7 +122,10 @@ class GELUMLP(nn.Module):
         self.fc2._residual_proj = True
 
     def forward(self, x):
-        return self.fc2(F.gelu(self.fc1(x), approximate="tanh"))
+        h = self.fc1(x)
+        # the native kernel pair on CUDA (same tanh approximation, fp32 arithmetic)
+        a = gelu_tanh(h) if gelu_supported(h) else F.gelu(h, approximate="tanh")
+        return self.fc2(a)
 
 
 class CADecoderBlock(nn.Module):

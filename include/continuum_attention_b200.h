@@ -221,9 +221,20 @@ int ca_add_rmsnorm_backward(const float* x_new, const float* w, const void* dy, 
                             const float* dx_new, float* dx, void* dr, float* dw, void* workspace,
                             size_t workspace_bytes, int64_t rows, int64_t D, void* stream);
 
-/* Number of kernels the last successful ca_forward / ca_backward //* Number of kernels the last successful ca_forward / ca_backward /
- * ca_rope_qkv_* / ca_rmsnorm_* / ca_add_rmsnorm_* call on this thread enqueued (memsets
- * excluded).  Diagnostic for launch accounting. */
+/*
+ * Tanh-approximate GELU, the CA-S decoder MLP's activation
+ * (cuda/continuum_attention.py:866-867, F.gelu(fc1(x), approximate='tanh')):
+ * y = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) elementwise over n
+ * contiguous elements, fp32 arithmetic; the backward gives dx = dy * gelu'(x).
+ * dtype CA_DTYPE_*; n a multiple of 16 bytes' worth of elements (4 fp32, 8
+ * bf16/fp16) and every buffer 16-byte aligned.  One launch each.
+ */
+int ca_gelu_tanh_forward(const void* x, void* y, int64_t n, int dtype, void* stream);
+int ca_gelu_tanh_backward(const void* x, const void* dy, void* dx, int64_t n, int dtype, void* stream);
+
+/* Number of kernels the last successful ca_forward / ca_backward /
+ * ca_rope_qkv_* / ca_rmsnorm_* / ca_add_rmsnorm_* / ca_gelu_tanh_* call on this
+ * thread enqueued (memsets excluded).  Diagnostic for launch accounting. */
 int ca_last_launch_count(void);
 
 /*

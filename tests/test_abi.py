@@ -102,3 +102,16 @@ def test_rmsnorm_argument_checks_on_cpu():
     assert b"null" in lib.ca_last_error()
     assert lib.ca_rmsnorm_forward(None, None, None, None, 0, 1024, 1e-6, 0, 1, None) == 0
     assert lib.ca_rmsnorm_workspace_size(0, 1024) == 0
+
+
+def test_gelu_argument_checks_on_cpu():
+    lib = _native.lib()
+    # rejected before any device work: unknown dtype, ragged length, null pointers
+    assert lib.ca_gelu_tanh_forward(None, None, 8, 7, None) == 1
+    assert lib.ca_gelu_tanh_forward(None, None, 6, 1, None) == 2
+    assert lib.ca_gelu_tanh_forward(None, None, 6, 0, None) == 2
+    assert lib.ca_gelu_tanh_forward(None, None, 8, 1, None) == 1
+    assert b"null" in lib.ca_last_error()
+    assert lib.ca_gelu_tanh_backward(None, None, None, 4, 0, None) == 1
+    assert lib.ca_gelu_tanh_forward(None, None, 0, 1, None) == 0
+    assert lib.ca_gelu_tanh_backward(None, None, None, 0, 2, None) == 0
