@@ -95,8 +95,8 @@ class ContinuumSelfAttention(nn.Module):
         self.head_dim = dim // heads
         self.rope_theta = rope_theta
         self.ca_query_tile = ca_query_tile
-        self.qkv = nn.Linear(dim, 3 * dim, bias=False)
-        self.out = nn.Linear(dim, dim, bias=False)
+        self.qkv = Linear(dim, 3 * dim, bias=False)
+        self.out = Linear(dim, dim, bias=False)
         self.out._residual_proj = True
         # variant S: positive trainable per-head score gain g = exp(rho), starting at 1
         self.log_qk_gain = nn.Parameter(torch.zeros(heads))
@@ -113,12 +113,48 @@ class ContinuumSelfAttention(nn.Module):
         return self.out(y.transpose(1, 2).reshape(B, T, C))
 
 
+class _WeightGradFp32(torch.autograd.Function):
+    """y = x W^T with W the fp32 master weight cast to bf16, as bf16 autocast runs
+    nn.Linear; the backward writes dW straight out of the GEMM in fp32 (bf16
+    operands, fp32 accumulate and store), where autocast stores a bf16 dW and then
+    converts it to fp32 in a separate pass over the weight."""
+
+    @staticmethod
+    def forward(ctx, x, weight):
+        wb = weight.to(torch.bfloat16)
+        xb = x.to(torch.bfloat16)
+        ctx.save_for_backward(xb, wb)
+        return F.linear(xb, wb)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xb, wb = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16)
+        dx = dy @ wb if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dw = torch.mm(dy.reshape(-1, dy.shape[-1]).t(), xb.reshape(-1, xb.shape[-1]), out_dtype=torch.float32)
+        return dx, dw
+
+
+class Linear(nn.Linear):
+    """nn.Linear (same parameters and state-dict keys) whose bias-free bf16-autocast
+    CUDA forward keeps the weight gradient in fp32 end to end (``_WeightGradFp32``);
+    every other case is nn.Linear itself."""
+
+    def forward(self, x):
+        if (self.bias is None and x.is_cuda and self.weight.dtype == torch.float32
+                and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+            return _WeightGradFp32.apply(x, self.weight)
+        return super().forward(x)
+
+
 class GELUMLP(nn.Module):
     def __init__(self, dim: int, ratio: float):
         super().__init__()
         hidden = int(dim * ratio)
-        self.fc1 = nn.Linear(dim, hidden, bias=False)
-        self.fc2 = nn.Linear(hidden, dim, bias=False)
+        self.fc1 = Linear(dim, hidden, bias=False)
+        self.fc2 = Linear(hidden, dim, bias=False)
         self.fc2._residual_proj = True
 
     def forward(self, x):
@@ -151,7 +187,7 @@ class ContinuumDecoderLM(nn.Module):
         self.byte_emb = nn.Embedding(cfg.vocab_size, cfg.d_model)
         self.blocks = nn.ModuleList([CADecoderBlock(cfg, attention_fn) for _ in range(cfg.n_layers)])
         self.norm_f = RMSNorm(cfg.d_model, cfg.eps)
-        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)   # not tied to byte_emb
+        self.lm_head = Linear(cfg.d_model, cfg.vocab_size, bias=False)   # not tied to byte_emb
         self.residual_init_scale = 1.0 / math.sqrt(2.0 * cfg.n_layers)
         self.apply(self._init_weights)
 

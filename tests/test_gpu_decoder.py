@@ -39,3 +39,29 @@ def test_training_steps_reduce_loss():
     assert losses[-1] < losses[0] - 0.5
     gains = torch.stack([b.attn.log_qk_gain.detach() for b in model.blocks])
     assert gains.abs().sum() > 0          # the learned gains moved
+
+
+def test_linear_weight_grad_in_fp32_matches_autocast_linear():
+    from continuum_attention_b200.decoder import Linear
+    torch.manual_seed(3)
+    ours = Linear(256, 512, bias=False).cuda()
+    ref = torch.nn.Linear(256, 512, bias=False).cuda()
+    ref.weight.data.copy_(ours.weight.data)
+    x = torch.randn(4, 96, 256, device="cuda")
+    dy = torch.randn(4, 96, 512, device="cuda")
+    outs = []
+    for m in (ours, ref):
+        xi = x.clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = m(xi)
+        y.backward(dy.to(y.dtype))
+        outs.append((y, xi.grad, m.weight.grad))
+    (y1, dx1, dw1), (y2, dx2, dw2) = outs
+    assert y1.dtype == y2.dtype == torch.bfloat16
+    assert torch.equal(y1, y2)                       # the same bf16 product as autocast
+    assert torch.equal(dx1, dx2)
+    assert dw1.dtype == torch.float32
+    # autocast's dW is the bf16 rounding of the fp32 accumulator this one keeps
+    exact = (dy.to(torch.bfloat16).double().reshape(-1, 512).t() @ x.to(torch.bfloat16).double().reshape(-1, 256))
+    assert ((dw1.double() - exact).abs() <= 1e-5 * exact.abs().max()).all()
+    assert ((dw2.double() - dw1.double()).abs() <= 2 ** -8 * dw1.double().abs() + 1e-6).all()
