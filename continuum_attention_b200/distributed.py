@@ -116,6 +116,23 @@ def train_step(model, optimizer, batch: torch.Tensor, amp_dtype=torch.bfloat16, 
         loss = model(batch, targets=batch)["loss"]
     loss.backward()
     if grad_clip and grad_clip > 0:
+        if _fused_adamw(optimizer):
+            # clip_grad_norm_'s scaling folded into the fused AdamW kernel, which
+            # divides each gradient by ``grad_scale`` as it reads it: one pass over
+            # the gradients fewer; scale = 1 / min(1, clip / (norm + 1e-6))
+            grads = [p.grad for p in model.parameters() if p.grad is not None]
+            norm = torch.nn.utils.get_total_norm(grads, 2.0)
+            optimizer.grad_scale = torch.clamp((norm.float() + 1e-6) / grad_clip, min=1.0)
+            try:
+                optimizer.step()
+            finally:
+                del optimizer.grad_scale
+            return loss.detach()
         torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip)
     optimizer.step()
     return loss.detach()
+
+
+def _fused_adamw(optimizer) -> bool:
+    return (type(optimizer) is torch.optim.AdamW and not hasattr(optimizer, "grad_scale")
+            and all(g.get("fused") for g in optimizer.param_groups))
