@@ -274,18 +274,21 @@ __device__ __forceinline__ void fwd_chunk_fast(const uint32_t (&cur)[16], int ch
     bprev = M1.y;
     sa = sb.y;
     ea = eb.y;
-    const uint32_t h2 = kBF16 ? pack_bf16x2(pv0, pv1) : pack_f16x2(pv0, pv1);
-    float h0, h1;
     if (kBF16) {
-      h0 = __uint_as_float(h2 << 16);
-      h1 = __uint_as_float(h2 & 0xffff0000u);
+      // hi = the upper 16 bits of each fp32 weight (a bf16 by truncation, one byte
+      // permute for the pair), lo = the exact fp32 remainder rounded to bf16: the
+      // pair still carries ~16 significant bits
+      const uint32_t u0 = __float_as_uint(pv0), u1 = __float_as_uint(pv1);
+      hi[x] = __byte_perm(u0, u1, 0x7632);
+      const float2 r = fma2(make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u)),
+                            neg1, make_float2(pv0, pv1));
+      lo[x] = pack_bf16x2(r.x, r.y);
     } else {
+      const uint32_t h2 = pack_f16x2(pv0, pv1);
       const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
-      h0 = __low2float(hh);
-      h1 = __high2float(hh);
+      hi[x] = h2;
+      lo[x] = pack_f16x2(pv0 - __low2float(hh), pv1 - __high2float(hh));
     }
-    hi[x] = h2;
-    lo[x] = kBF16 ? pack_bf16x2(pv0 - h0, pv1 - h1) : pack_f16x2(pv0 - h0, pv1 - h1);
   }
   tmem_st8(t_p + 16 * ch, hi);       // P hi and lo of these 16 keys replace their own S columns
   tmem_st8(t_p + 16 * ch + 8, lo);

@@ -115,11 +115,19 @@ def train_step(model, optimizer, batch: torch.Tensor, amp_dtype=torch.bfloat16, 
     with torch.autocast(dev_type, dtype=amp_dtype, enabled=amp_dtype is not None):
         loss = model(batch, targets=batch)["loss"]
     loss.backward()
+    clip_and_step(model, optimizer, grad_clip)
+    return loss.detach()
+
+
+def clip_and_step(model, optimizer, grad_clip: float = 1.0):
+    """``clip_grad_norm_(model.parameters(), grad_clip)`` then ``optimizer.step()``.
+
+    With a fused AdamW the clip's scaling is folded into the optimizer kernel,
+    which divides each gradient by ``grad_scale`` as it reads it: one pass over
+    the gradients fewer; grad_scale = 1 / min(1, grad_clip / (norm + 1e-6)).
+    """
     if grad_clip and grad_clip > 0:
         if _fused_adamw(optimizer):
-            # clip_grad_norm_'s scaling folded into the fused AdamW kernel, which
-            # divides each gradient by ``grad_scale`` as it reads it: one pass over
-            # the gradients fewer; scale = 1 / min(1, clip / (norm + 1e-6))
             grads = [p.grad for p in model.parameters() if p.grad is not None]
             norm = torch.nn.utils.get_total_norm(grads, 2.0)
             optimizer.grad_scale = torch.clamp((norm.float() + 1e-6) / grad_clip, min=1.0)
@@ -127,10 +135,9 @@ def train_step(model, optimizer, batch: torch.Tensor, amp_dtype=torch.bfloat16, 
                 optimizer.step()
             finally:
                 del optimizer.grad_scale
-            return loss.detach()
+            return
         torch.nn.utils.clip_grad_norm_(model.parameters(), grad_clip)
     optimizer.step()
-    return loss.detach()
 
 
 def _fused_adamw(optimizer) -> bool:
