@@ -987,18 +987,20 @@ __device__ __forceinline__ void bwd_keys8_fast(const uint32_t (&sv)[16], const u
     const float sBy = (x < 3) ? sA[x + 1].x : s8;
     const float gBy = (x < 3) ? gA[x + 1].x : g8;
     const float2 EB = make_float2(e[2 * x + 1], e[2 * x + 2]);
-    const float2 d = make_float2(sA[x].y - sA[x].x, sBy - sA[x].y);
-    const float2 nd = mul2(d, neg1);
-    const float2 r = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    // nd = -(b - a) straight from the two subtractions; 1/d takes the negation as
+    // the reciprocal's operand, and the series below runs in nd with alternating
+    // signs (every value bit-identical to working with d)
+    const float2 nd = make_float2(sA[x].x - sA[x].y, sA[x].y - sBy);
+    const float2 r = make_float2(rcp_approx(-nd.x), rcp_approx(-nd.y));
     const float2 m0c = mul2(make_float2(EB.x - e[2 * x], EB.y - e[2 * x + 1]), r);
     const float2 m1c = mul2(fma2(m0c, neg1, EB), r);
     const float2 m2c = mul2(fma2(m1c, neg2, EB), r);
-    float2 ser = fma2(splat2(1.f / 36.f), d, splat2(1.f / 10.f));
-    ser = fma2(ser, d, splat2(1.f / 4.f));
-    ser = fma2(ser, d, splat2(1.f / 3.f));
+    float2 ser = fma2(splat2(-1.f / 36.f), nd, splat2(1.f / 10.f));
+    ser = fma2(ser, nd, splat2(-1.f / 4.f));
+    ser = fma2(ser, nd, splat2(1.f / 3.f));
     float2 M2;
-    M2.x = fabsf(d.x) < kSeriesMaxBwd ? e[2 * x] * ser.x : m2c.x;
-    M2.y = fabsf(d.y) < kSeriesMaxBwd ? e[2 * x + 1] * ser.y : m2c.y;
+    M2.x = fabsf(nd.x) < kSeriesMaxBwd ? e[2 * x] * ser.x : m2c.x;
+    M2.y = fabsf(nd.y) < kSeriesMaxBwd ? e[2 * x + 1] * ser.y : m2c.y;
     const float2 M1 = mul2(fma2(nd, M2, EB), half);
     const float2 M0 = fma2(nd, M1, EB);
     const float2 A = fma2(M1, neg1, M0);
