@@ -95,7 +95,8 @@ def _pci_bus_id(local: int) -> str:
 def _gpu_local_cpus(local: int):
     """Run the block on the host CPUs NVML reports as local to GPU `local`, so that
     pinned host buffers allocated inside sit on that GPU's NUMA node; the previous
-    CPU affinity is restored afterwards.  Yields whether the binding took effect."""
+    CPU affinity is restored afterwards.  Yields whether the block runs on GPU-local
+    CPUs (bound here, or the process's CPUs were all local already)."""
     old = os.sched_getaffinity(0)
     bound = False
     try:
@@ -107,7 +108,7 @@ def _gpu_local_cpus(local: int):
             cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (int(m) >> b) & 1} & old
             if cpus and cpus != old:
                 os.sched_setaffinity(0, cpus)
-                bound = True
+            bound = bool(cpus)     # running on GPU-local CPUs (bound here, or already all local)
         finally:
             pynvml.nvmlShutdown()
     except Exception:
