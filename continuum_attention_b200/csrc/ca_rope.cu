@@ -16,10 +16,9 @@
 // and its transpose for the gradient.  The caller passes the (c, s) table as
 // float32 [T][D/2][2]; arithmetic is fp32 with one rounding per output.
 //
-// Work unit: one block per token (b, t), one thread per 8-element chunk of its
-// [3][H][D] projection row; the projection-side access is fully contiguous, the
-// [B,H,T,D] side writes or reads whole D-element rows.  HBM-bound: 2 x 3*B*T*H*D
-// elements per pass.
+// Work unit: one thread per 8-element chunk of a token's [3][H][D] projection row;
+// a block takes one token forward, G consecutive tokens backward.  HBM-bound:
+// 2 x 3*B*T*H*D elements per pass.
 #include "ca_common.cuh"
 #include "ca_internal.h"
 
@@ -67,9 +66,21 @@ __device__ __forceinline__ void load8<__half>(const __half* p, float (&x)[8]) { 
 template <>
 __device__ __forceinline__ void store8<__half>(__half* p, const float (&x)[8]) { store8_16(p, x); }
 
-// One block per token (b, t); thread j of the token's 3*H*D/8 chunks takes
-// chunk c = j % (D/8) of head h = (j / (D/8)) % H of q, k or v (j / (H*D/8)):
-// 32-bit index arithmetic once per chunk instead of a 64-bit decomposition.
+// Forward: one block per token (b, t); thread j of the token's 3*H*D/8 chunks takes
+// chunk c = j % (D/8) of head h = (j / (D/8)) % H of q, k or v (j / (H*D/8)), so a
+// warp reads one contiguous run of the projection row.  Backward: a block of G =
+// 32 / (D/8) consecutive tokens; element j of its [3][H][G][D/8] chunk grid is
+// chunk c of head h for token tt, so a warp reads G consecutive [B,H,T,D] rows of
+// one head.  Reading contiguously measured faster than writing contiguously, each
+// way.  32-bit index arithmetic once per chunk.
+
+// tokens per backward block for head dim D
+__host__ __device__ __forceinline__ unsigned tokens_per_block(unsigned D) {
+  const unsigned chunks = D / 8;
+  if (chunks == 0 || 32 % chunks) return 1;
+  const unsigned g = 32 / chunks;
+  return g > 8 ? 8 : g;
+}
 
 // qkv [B][T][3][H][D] -> q, k (rotated), v [B][H][T][D]
 template <typename T>
@@ -103,15 +114,19 @@ __global__ void pack_fwd_kernel(const T* __restrict__ qkv, const float2* __restr
 // dq, dk, dv [B][H][T][D] -> dqkv [B][T][3][H][D] (transposed rotation on dq, dk)
 template <typename T>
 __global__ void pack_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv,
-                                const float2* __restrict__ cs, T* __restrict__ dqkv, int Tn, int H, int D) {
+                                const float2* __restrict__ cs, T* __restrict__ dqkv, int ntok, int Tn, int H, int D,
+                                int G) {
   pdl_wait();
   pdl_launch_dependents();
-  const unsigned chunks = (unsigned)D / 8, per_head = chunks, per_which = (unsigned)H * chunks;
-  const unsigned token = blockIdx.x, t = token % (unsigned)Tn, b = token / (unsigned)Tn;
-  T* dst = dqkv + (size_t)token * 3 * per_which * 8;
+  const unsigned chunks = (unsigned)D / 8;
+  const unsigned per_head = G * chunks, per_which = (unsigned)H * per_head;
   for (unsigned j = threadIdx.x; j < 3 * per_which; j += blockDim.x) {
     const unsigned which = j / per_which, rem = j - which * per_which;
-    const unsigned h = rem / per_head, c = rem - h * per_head;
+    const unsigned h = rem / per_head, r2 = rem - h * per_head;
+    const unsigned tt = r2 / chunks, c = r2 - tt * chunks;
+    const unsigned token = blockIdx.x * (unsigned)G + tt;
+    if (token >= (unsigned)ntok) continue;
+    const unsigned t = token % (unsigned)Tn, b = token / (unsigned)Tn;
     const T* src = which == 0 ? dq : (which == 1 ? dk : dv);
     float x[8];
     load8<T>(src + (((size_t)b * H + h) * Tn + t) * D + 8 * c, x);
@@ -125,29 +140,31 @@ __global__ void pack_bwd_kernel(const T* __restrict__ dq, const T* __restrict__ 
         x[2 * p + 1] = fmaf(o, w.x, -e * w.y);
       }
     }
-    store8<T>(dst + (size_t)j * 8, x);
+    store8<T>(dqkv + ((size_t)token * 3 * H + which * H + h) * D + 8 * c, x);
   }
 }
 
-// threads per token block: the token's chunk count rounded up to whole warps, at most 1024
-static unsigned block_for(long long H, long long D) {
-  const long long n = 3 * H * (D / 8);
+// threads per block of G tokens: the block's chunk count rounded up to whole warps, at most 512
+static unsigned block_for(long long H, long long D, long long G) {
+  const long long n = 3 * H * (D / 8) * G;
   const long long w = (n + 31) / 32 * 32;
-  return (unsigned)(w < 1024 ? w : 1024);
+  return (unsigned)(w < 512 ? w : 512);
 }
 
 template <typename T>
 static cudaError_t fwd_t(const void* qkv, const float* cs, void* q, void* k, void* v, long long B, long long Tn,
                          long long H, long long D, cudaStream_t s) {
-  return launch_pdl(pack_fwd_kernel<T>, dim3((unsigned)(B * Tn)), dim3(block_for(H, D)), 0, s, (const T*)qkv,
+  return launch_pdl(pack_fwd_kernel<T>, dim3((unsigned)(B * Tn)), dim3(block_for(H, D, 1)), 0, s, (const T*)qkv,
                     (const float2*)cs, (T*)q, (T*)k, (T*)v, (int)Tn, (int)H, (int)D);
 }
 
 template <typename T>
 static cudaError_t bwd_t(const void* dq, const void* dk, const void* dv, const float* cs, void* dqkv, long long B,
                          long long Tn, long long H, long long D, cudaStream_t s) {
-  return launch_pdl(pack_bwd_kernel<T>, dim3((unsigned)(B * Tn)), dim3(block_for(H, D)), 0, s, (const T*)dq,
-                    (const T*)dk, (const T*)dv, (const float2*)cs, (T*)dqkv, (int)Tn, (int)H, (int)D);
+  const long long G = tokens_per_block((unsigned)D);
+  return launch_pdl(pack_bwd_kernel<T>, dim3((unsigned)((B * Tn + G - 1) / G)), dim3(block_for(H, D, G)), 0, s,
+                    (const T*)dq, (const T*)dk, (const T*)dv, (const float2*)cs, (T*)dqkv, (int)(B * Tn), (int)Tn,
+                    (int)H, (int)D, (int)G);
 }
 
 cudaError_t forward(const void* qkv, const float* cos_sin, void* q, void* k, void* v, long long B, long long T,
