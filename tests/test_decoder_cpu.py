@@ -51,3 +51,32 @@ def test_decoder_is_causal():
     with torch.no_grad():
         a, b = model(x)["logits"], model(x2)["logits"]
     assert (a[:, :T // 2 + 1] - b[:, :T // 2 + 1]).abs().max().item() <= 1e-5
+
+
+def test_linear_is_nn_linear_off_the_bf16_cuda_path():
+    # decoder.Linear keeps nn.Linear's parameters and state-dict keys; outside bf16
+    # autocast on CUDA it is nn.Linear itself
+    from continuum_attention_b200.decoder import Linear
+    torch.manual_seed(2)
+    ours, ref = Linear(16, 8, bias=False), torch.nn.Linear(16, 8, bias=False)
+    ref.load_state_dict(ours.state_dict())
+    assert list(ours.state_dict()) == list(ref.state_dict())
+    x = torch.randn(3, 16, requires_grad=True)
+    xr = x.detach().clone().requires_grad_(True)
+    ours(x).sum().backward()
+    ref(xr).sum().backward()
+    assert torch.equal(x.grad, xr.grad) and torch.equal(ours.weight.grad, ref.weight.grad)
+
+
+def test_clip_and_step_matches_clip_grad_norm_without_fused_adamw():
+    from continuum_attention_b200.distributed import build_adamw, clip_and_step
+    a, b = _tiny(1), _tiny(1)
+    oa, ob = build_adamw(a, lr=1e-2), build_adamw(b, lr=1e-2)
+    batch = torch.randint(0, 256, (2, 32))
+    for m in (a, b):
+        m(batch, targets=batch)["loss"].backward()
+    clip_and_step(a, oa, 0.05)                 # CPU parameters: the unfused optimizer path
+    torch.nn.utils.clip_grad_norm_(b.parameters(), 0.05)
+    ob.step()
+    for pa, pb in zip(a.parameters(), b.parameters()):
+        assert torch.equal(pa, pb)
