@@ -27,8 +27,11 @@ BASELINE config 3 at B = 8, [8,16,16384,64], its 128 head-sequences split over t
 ranks (strong scaling, ``--no-config3`` skips it).
 
 ``--impl reference`` times the reference algorithm's CPU path (the float32
-restatement in oracle/, all host threads) on a bounded sample of the same
-workload and prints the same line with "impl": "reference".
+restatement in oracle/, all host threads) on the same workload, one whole
+config-2 batch per step with the same --steps / --warmup, and prints the same
+line with "impl": "reference".  At N=1 the GPU arm's line also carries
+"reference_cuda": the reference's own CUDA kernels (built from its sources into
+oracle/_ref) timed at config 2 on the same GPU, outside the timed region.
 """
 from __future__ import annotations
 
@@ -205,21 +208,18 @@ def _max_over_ranks(world, x: float) -> float:
     return float(t.item())
 
 
-def cpu_reference_sample(steps: int, warmup: int, sample_heads: int = 1):
-    """Time the reference algorithm's CPU path (oracle restatement, float32).
+def cpu_reference_sample(steps: int, warmup: int, shape=SHAPE):
+    """Time the reference algorithm's CPU path (oracle restatement, float32, all host threads).
 
-    Each step is one forward+backward of ``sample_heads`` head-sequences of the
-    config-2 workload ([1, sample_heads, 2048, 64]); throughput is scaled by the
-    FLOPs the sample processes.  Returns (tflops, median_s, threads, sample).
+    Each step is one forward+backward of ``shape`` (default: the whole config-2 batch,
+    [2,16,2048,64]).  Returns (tflops, median_s, threads, sample).
     """
     from oracle.ca_oracle import ca_forward_backward
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    B, H, T, D = SHAPE
     g = torch.Generator().manual_seed(2)
-    shape = (1, sample_heads, T, D)
     q, k, v, dy = (torch.randn(shape, generator=g) for _ in range(4))
-    lg = torch.zeros(sample_heads)
+    lg = torch.zeros(shape[1])
     times = []
     for it in range(warmup + steps):
         t0 = time.perf_counter()
@@ -228,27 +228,91 @@ def cpu_reference_sample(steps: int, warmup: int, sample_heads: int = 1):
         if it >= warmup:
             times.append(dt)
     med = statistics.median(times)
-    f = 4.0 * sample_heads * T * T * D
-    sample = (f"[1,{sample_heads},{T},{D}] fp32 fwd+bwd of the config-2 workload per step "
-              f"(oracle/ca_oracle.py, query tile 128), median of {len(times)}")
-    return f / med / 1e12, med, threads, sample
+    sample = (f"{list(shape)} fp32 fwd+bwd per step (oracle/ca_oracle.py, the reference's tiled CPU "
+              f"algorithm restated, query tile 128), median of {len(times)}")
+    return flops_per_step(shape) / med / 1e12, med, threads, sample
+
+
+def _config(world: int, kernels: str):
+    """The workload description both arms print (BASELINE config 2 per rank)."""
+    B, H, T, D = SHAPE
+    return {"workload": "CA operator fwd+bwd, BASELINE config 2 ([2,16,2048,64] bf16, gain 1, causal) "
+                        "per rank; operator sharded over B*H, no collective",
+            "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
+            "parallelism": f"bh-shard x{world}", "kernels": kernels,
+            "l2": f"{N_INPUT_SETS} rotating input sets (~{N_INPUT_SETS * 92} MB) > 126 MB L2",
+            "vs_baseline_ref": "reference CUDA v6, 1x V100 fp16, 16.603 ms (README.md:97)"}
 
 
 def run_reference_arm(args, world, rank):
+    """The reference's CPU path on the host cores of rank 0 over the whole config-2 batch,
+    with the same --steps and --warmup as the GPU arm (about 5-15 s per step on 8-16
+    cores).  The reference itself is Python and is not present on the GPU box, so its
+    restatement in oracle/ (pinned to the reference's outputs by tests/test_oracle.py)
+    stands in: "kind": "port"."""
     if rank != 0:
         return
-    tflops, med, threads, sample = cpu_reference_sample(max(1, min(args.steps, 5)), min(args.warmup, 1))
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    tflops, med, threads, sample = cpu_reference_sample(steps, warmup)
     line = {
         "metric": METRIC, "value": tflops, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-        "steps": max(1, min(args.steps, 5)), "warmup": min(args.warmup, 1),
-        "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "CA operator fwd+bwd, BASELINE config 2 shape, reference CPU path sample",
-                   "shape": list(SHAPE), "parallelism": "host cores of rank 0"},
+        "steps": steps, "warmup": warmup, "ms_per_step": med * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config(world, args.kernels),
         "cpu_baseline": {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tflops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_reference_cuda(local):
+    """The reference's own CUDA kernels (oracle/_ref, built from its sources) at config 2
+    on this GPU, timed like the reference's speed phase (cuda/benchmark.py:111-125):
+    CUDA events around the op and around autograd.grad, medians over 7 repeats with 2
+    input sets.  None when oracle/_ref is not built."""
+    from oracle import ref_cuda
+    if not ref_cuda.available():
+        return None
+    import continuum_attention_b200 as ca
+    dev = torch.device("cuda", local)
+    out = {"shape": list(SHAPE), "query_tile": 128, "source": "oracle/_ref (reference sources, compiled here)"}
+    runs = (("reference_prefix_v6_fp16", lambda q, k, v, lg: ref_cuda.ref_continuum_attention(q, k, v, lg, 128,
+                                                                                            "prefix_v6"),
+             torch.float16),
+            ("reference_prefix_bf16", lambda q, k, v, lg: ref_cuda.ref_continuum_attention(q, k, v, lg, 128,
+                                                                                         "prefix"),
+             torch.bfloat16),
+            ("ours_bf16", lambda q, k, v, lg: ca.continuum_attention(q, k, v, lg, 128), torch.bfloat16))
+    for name, fn, dtype in runs:
+        sets = []
+        for sd in range(2):
+            g = torch.Generator(device="cpu").manual_seed(1649 + sd)
+            q, k, v, dy = (torch.randn(SHAPE, generator=g).to(dev, dtype) for _ in range(4))
+            lg = torch.zeros(SHAPE[1], device=dev)
+            sets.append(tuple(t.requires_grad_(True) for t in (q, k, v, lg)) + (dy,))
+
+        def step(i):
+            q, k, v, lg, dy = sets[i % 2]
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            y = fn(q, k, v, lg)
+            ev[1].record()
+            torch.autograd.grad((y.float() * dy.float()).sum(), (q, k, v, lg))
+            ev[2].record()
+            return ev
+
+        for i in range(2):
+            step(i)
+        torch.cuda.synchronize()
+        evs = [step(i) for i in range(7)]
+        torch.cuda.synchronize()
+        med = lambda a, b: statistics.median(e[a].elapsed_time(e[b]) for e in evs)
+        out[name] = {"forward_ms": med(0, 1), "backward_ms": med(1, 2), "total_ms": med(0, 2)}
+        del sets
+    torch.cuda.empty_cache()
+    out["speedup_vs_prefix_v6_fp16"] = (out["reference_prefix_v6_fp16"]["total_ms"] /
+                                        out["ours_bf16"]["total_ms"])
+    return out
 
 
 def _make_sets(n, device, dtype, seed):
@@ -523,13 +587,14 @@ def run_ours(args, world, rank, local):
     n_elem = B * H * T * (T + 1) / 2
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                 "frac": achieved / peak_tflops, "traffic": traffic,
+                "traffic_source": "ncu capture of this kernel at this shape, fixed figure from profiles/ (not this run)",
                 "kernel": f"ca_{dom} ({impl})", "peak_source": f"{peak_kind} bf16 dense burst",
                 "fwd_ms": fwd_avg, "bwd_ms": bwd_avg,
                 "mufu_note": f"{n_elem:.4g} causal score elements per step; >= 2 MUFU ops each per direction"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tflops, med, threads, sample = cpu_reference_sample(3, 1)
+        tflops, med, threads, sample = cpu_reference_sample(2, 0)
         cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
     clocks = clk.summary()
@@ -547,18 +612,14 @@ def run_ours(args, world, rank, local):
         decoder = run_decoder(args, world, rank, local, steps=args.decoder_steps, warmup=3)
     tinylm = run_tinylm(local) if (world == 1 and not args.no_tinylm) else None
     config3 = None if args.no_config3 else run_config3_sharded(world, rank, local)
+    ref_cuda = run_reference_cuda(local) if (world == 1 and not args.no_reference_cuda) else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / (flops_per_step() / (PUBLISHED_V100_V6_MS * 1e-3) / 1e12),
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "CA operator fwd+bwd, BASELINE config 2 ([2,16,2048,64] bf16, gain 1, causal) "
-                                   "per rank; operator sharded over B*H, no collective",
-                       "global_batch": SHAPE[0] * world, "seq_len": T, "heads": H, "head_dim": D,
-                       "parallelism": f"bh-shard x{world}", "kernels": impl,
-                       "l2": f"{N_INPUT_SETS} rotating input sets (~{N_INPUT_SETS * 92} MB) > 126 MB L2",
-                       "vs_baseline_ref": "reference CUDA v6, 1x V100 fp16, 16.603 ms (README.md:97)"},
+            "config": _config(world, impl),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "host_buffers_numa_local": numa_bound,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
@@ -570,6 +631,7 @@ def run_ours(args, world, rank, local):
             "decoder": decoder,
             "tinylm": tinylm,
             "config3_sharded": config3,
+            "reference_cuda": ref_cuda,
         }
         print(json.dumps(line), flush=True)
 
@@ -586,6 +648,8 @@ def main():
     p.add_argument("--decoder-steps", type=int, default=10)
     p.add_argument("--no-tinylm", action="store_true", help="skip the TinyLM-P small-model measurement")
     p.add_argument("--no-config3", action="store_true", help="skip the config-3 strong-scaling measurement")
+    p.add_argument("--no-reference-cuda", action="store_true",
+                   help="skip timing the reference's CUDA kernels (oracle/_ref) at config 2")
     args = p.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

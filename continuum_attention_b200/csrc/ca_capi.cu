@@ -219,6 +219,11 @@ static int check_rope(const char* fn, const void* a, const void* b, const void* 
     return fail(CA_ERR_INVALID_ARGUMENT, "%s: unknown dtype code %d", fn, dtype);
   if (D % 8 != 0 || D > 256)
     return fail(CA_ERR_UNSUPPORTED, "%s: head dim D=%lld must be a multiple of 8 and <= 256", fn, (long long)D);
+  // the kernels index tokens (b*T + t) and per-token work items (3*H*D/8) in 32 bits
+  if (T > 0x7fffffffLL || (T > 0 && B > 0x7fffffffLL / T))
+    return fail(CA_ERR_UNSUPPORTED, "%s: B*T=%lld*%lld tokens exceed 2^31-1", fn, (long long)B, (long long)T);
+  if (H > (1LL << 20))
+    return fail(CA_ERR_UNSUPPORTED, "%s: H=%lld heads exceed 2^20", fn, (long long)H);
   if (B * T * H * D == 0) return CA_OK;
   if (!a || !b || !c || !d || !cs) return fail(CA_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
   const uintptr_t m = (uintptr_t)a | (uintptr_t)b | (uintptr_t)c | (uintptr_t)d | (uintptr_t)cs;
@@ -434,14 +439,19 @@ int ca_device_status(int reset) {
 //     library keeps it until the process exits;
 //   - a problem whose scratch need (ca_backward_workspace_size) exceeds it is
 //     rejected with CA_ERR_UNSUPPORTED and a message naming both sizes;
-//   - the first call on a device looks up the array's device address there
-//     (cudaGetSymbolAddress) and caches it, so make that first call before any
-//     stream capture on that device;
+//   - the first call in a device's context looks up the array's device address
+//     there (cudaGetSymbolAddress) and caches it under that context's id, so
+//     make that first call before any stream capture on that device; a context
+//     torn down and rebuilt (cudaDeviceReset, or a framework that recreates its
+//     context) has a new id, and the next call looks the address up again -- that
+//     call, too, belongs before any stream capture;
 //   - all calls on a device share the one array and leave their contents in
 //     it; the backward clears what must start at zero (the dQ accumulator)
 //     itself, but two calls whose work overlaps on the GPU (different streams
 //     with no ordering between them) race on the array and give wrong results;
 //   - nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <cuda.h>
+
 #include <mutex>
 
 namespace {
@@ -451,10 +461,45 @@ constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+  bool valid;
+  unsigned long long ctx_id;   // id of the context the address belongs to
+  void* ptr;
+};
 
-// Device address of g_noalloc_scratch on the current device, looked up once per device.
+std::mutex g_noalloc_mutex;
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (cuCtxGetId, through the
+// runtime's driver entry points); false when there is none or the driver lacks the call.
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    looked_up = true;
+  }
+  if (!get_current || !get_id) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of g_noalloc_scratch in the current device's context.  Looked
+// up once per context and cached under the context's id; without a context id
+// (a driver that lacks cuCtxGetId) it is looked up on every call.
 int noalloc_scratch_here(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -462,14 +507,19 @@ int noalloc_scratch_here(void** out) {
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     return fail(CA_ERR_UNSUPPORTED, "ca_backward_noalloc: device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "ca_backward_noalloc: cudaGetSymbolAddress of the scratch array");
-    if (!p) return fail(CA_ERR_CUDA, "ca_backward_noalloc: scratch array has no device address");
-    g_noalloc_ptr[dev] = p;
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  unsigned long long id = 0;
+  if (slot.valid && current_context_id(&id) && id == slot.ctx_id) {
+    *out = slot.ptr;
+    return CA_OK;
   }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // makes the device's context current if it is not
+  if (e != cudaSuccess) return cuda_fail(e, "ca_backward_noalloc: cudaGetSymbolAddress of the scratch array");
+  if (!p) return fail(CA_ERR_CUDA, "ca_backward_noalloc: scratch array has no device address");
+  slot.ptr = p;
+  slot.valid = current_context_id(&slot.ctx_id);
+  *out = p;
   return CA_OK;
 }
 

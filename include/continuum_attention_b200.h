@@ -152,8 +152,11 @@ int ca_backward_ex(const void* q, const void* k, const void* v, const void* o, c
  * not call cudaMalloc afterwards.  The scratch is a fixed 32 MiB array inside
  * the library (held on every GPU that loads it until the process exits);
  * problems whose ca_backward_workspace_size() exceeds it return
- * CA_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
- * address, so make it before any stream capture on that device.  All calls on
+ * CA_ERR_UNSUPPORTED.  The first call in a device's context looks up the
+ * array's device address and caches it under the context's id, so make it
+ * before any stream capture on that device; after the context is torn down and
+ * rebuilt (cudaDeviceReset) the next call looks it up again and belongs before
+ * any capture as well.  All calls on
  * a device share the array: calls whose GPU work overlaps (unordered streams)
  * race and produce wrong results.  It allocates nothing.
  */

@@ -115,3 +115,18 @@ def test_gelu_argument_checks_on_cpu():
     assert lib.ca_gelu_tanh_backward(None, None, None, 4, 0, None) == 1
     assert lib.ca_gelu_tanh_forward(None, None, 0, 1, None) == 0
     assert lib.ca_gelu_tanh_backward(None, None, None, 0, 2, None) == 0
+
+
+def test_rope_argument_checks_on_cpu():
+    lib = _native.lib()
+    fake = ctypes.c_void_p(256)
+    # token and head counts beyond the kernels' 32-bit indexing are rejected before any device work
+    st, msg = _status_and_msg(lib.ca_rope_qkv_forward(fake, fake, fake, fake, fake, 2, 1 << 30, 1, 8, 1, None))
+    assert st == 2 and "2^31-1" in msg
+    st, msg = _status_and_msg(lib.ca_rope_qkv_backward(fake, fake, fake, fake, fake, 1, 1 << 31, 1, 8, 1, None))
+    assert st == 2 and "2^31-1" in msg
+    st, msg = _status_and_msg(lib.ca_rope_qkv_forward(fake, fake, fake, fake, fake, 1, 4, (1 << 20) + 1, 8, 1, None))
+    assert st == 2 and "heads" in msg
+    st, msg = _status_and_msg(lib.ca_rope_qkv_forward(fake, fake, fake, fake, fake, 1, 4, 2, 12, 1, None))
+    assert st == 2 and "multiple of 8" in msg
+    assert lib.ca_rope_qkv_forward(None, None, None, None, None, 0, 4, 2, 8, 1, None) == 0
