@@ -88,6 +88,30 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
 
+// a - b on packed fp32 pairs, each lane rounded like its scalar counterpart
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+// max(a, b, c) in one instruction (three-input max, sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// closed if |nd| >= thr, else ea * ps: the series branch of a moment select, as a
+// compare and one predicated multiply (no separate product and select)
+__device__ __forceinline__ float sel_series(float closed, float nd, float ea, float ps, float thr) {
+  float r;
+  asm("{\n\t.reg .pred p;\n\t.reg .f32 t;\n\tabs.f32 t, %2;\n\tsetp.lt.f32 p, t, %5;\n\t"
+      "mov.f32 %0, %1;\n\t@p mul.f32 %0, %3, %4;\n\t}"
+      : "=f"(r) : "f"(closed), "f"(nd), "f"(ea), "f"(ps), "f"(thr));
+  return r;
+}
+
 // J_1(d) by its power series: sum_{k<10} d^k / (k! (k+2)).
 __device__ __forceinline__ float series_j1(float d) {
   float p = 1.f / 3991680.f;
@@ -201,8 +225,7 @@ __device__ __forceinline__ void seg_moments012_sel(float Ea, float Eb, float d, 
   const float m0c = (Eb - Ea) * r;
   const float m1c = (Eb - m0c) * r;
   const float m2c = fmaf(-2.f, m1c, Eb) * r;
-  const float m2s = Ea * series_j2_bwd(d);
-  M2 = fabsf(d) < kSeriesMaxBwd ? m2s : m2c;
+  M2 = sel_series(m2c, d, Ea, series_j2_bwd(d), kSeriesMaxBwd);
   M1 = 0.5f * fmaf(-d, M2, Eb);
   M0 = fmaf(-d, M1, Eb);
 }

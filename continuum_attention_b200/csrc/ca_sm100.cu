@@ -32,6 +32,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "ca_common.cuh"
 #include "ca_internal.h"
@@ -104,7 +105,15 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint3
 //   order, so it overwrites P_h only after P V'_h has read it) -> refill the ring
 //   stage of h with half-tile h+4 once P V'_h has completed.  The math warps thus
 //   find S of their next half-tile already computed.
-template <bool kBF16>
+// K half-tile h into ring stage st: rows h*64 .. h*64+63 of head-sequence bh, through
+// the permuted 5-D view (kPerm: (D, s, j, chunk, bh), see fwd_chunk_perm) or the 3-D one.
+template <bool kPerm>
+__device__ __forceinline__ void load_k_half(void* dst, const CUtensorMap* tk, uint64_t* bar, int h, int bh) {
+  if (kPerm) tma_load_5d(dst, tk, bar, 0, 0, 0, h * (HB / 16), bh);
+  else tma_load_3d(dst, tk, bar, 0, h * HB, bh);
+}
+
+template <bool kBF16, bool kPerm>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv, int bh,
                          int q0, int nh, uint32_t tmem) {
   volatile int* ab = &sm.abort_flag;
@@ -122,7 +131,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   tma_load_3d(sm.q, tq, &sm.bar_q, 0, q0, bh);
   for (int t = 0; t < KSTAGES && t < nh; ++t) {
     mbar_arrive_expect_tx(&sm.bar_k[t], HALF_BYTES);
-    tma_load_3d(sm.k[t], tk, &sm.bar_k[t], 0, t * HB, bh);
+    load_k_half<kPerm>(sm.k[t], tk, &sm.bar_k[t], t, bh);
     mbar_arrive_expect_tx(&sm.bar_v[t], HALF_BYTES);
     tma_load_3d(sm.v[t], tv, &sm.bar_v[t], 0, t * HB - 1, bh);
     k_pending[t] = v_pending[t] = true;
@@ -163,7 +172,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     if (hr < nh) {
       if (!mbar_wait_warp(&sm.bar_kv_free[st], (h / KSTAGES) & 1, ab)) break;
       mbar_arrive_expect_tx(&sm.bar_k[st], HALF_BYTES);
-      tma_load_3d(sm.k[st], tk, &sm.bar_k[st], 0, hr * HB, bh);
+      load_k_half<kPerm>(sm.k[st], tk, &sm.bar_k[st], hr, bh);
       mbar_arrive_expect_tx(&sm.bar_v[st], HALF_BYTES);
       tma_load_3d(sm.v[st], tv, &sm.bar_v[st], 0, hr * HB - 1, bh);
       k_pending[st] = v_pending[st] = true;
@@ -214,7 +223,9 @@ __device__ __forceinline__ void fwd_chunk(const uint32_t (&cur)[16], int ch, flo
         // column 0 holds key j0-1: with 64-key half-tiles that is row i's own key
         // for i = q0+63 (for j0 = 0 it is key -1, and ea = 0 there)
         const int key = j0 - 1 + c;
-        const float cap = 0.5f * ea * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
+        // a select, not a product: ea of a key beyond row i may have overflowed
+        const float nc = (key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f);
+        const float cap = nc > 0.f ? 0.5f * nc * ea : 0.f;
         p += cap;
         z += cap;
       }
@@ -318,6 +329,306 @@ __device__ __forceinline__ int fwd_chunk_kind(int ch, int kb, int q0, int warp, 
   if (kb + 16 * ch + 15 <= q0 + 32 * warp) return 1;
   if (kb + 16 * ch - 1 > q0 + 32 * warp + 31) return 0;
   return 2;
+}
+
+// ---- permuted-key form (T a multiple of 16) ----
+// K half-tiles are staged through a 5-D view of K that puts key kc+j+8s of every
+// 16-key chunk (kc = first key of the chunk) in shared-memory row 2j+s.  S column
+// 2j+s of the chunk then holds key kc+j+8s, so the register pair (2j, 2j+1) of the
+// chunk's sixteen TMEM columns is the key pair (j, j+8), and the left neighbours
+// (j-1, j+7) of pair j are pair j-1 (pair 0's are the previous chunk's last key and
+// key 7).  Every quantity that pairs a key with its left neighbour -- the score
+// difference, Ea - Eb, Ea * series, B_{k-1} + A_k -- is then one packed f32x2
+// operation for two keys.  P goes back to TMEM in natural key order (hi/lo bf16
+// pairs), so V' is staged unpermuted as before.
+//
+// 16 keys of one row, keys kc..kc+15 in permuted order in raw[0..15]; output
+// slot t = weight of key kc-1+t (pair j: slots j and j+8).  On entry (sa, ea,
+// bprev) are the scaled score, exponential and right share B of key kc-1.
+// kEdge: keys beyond row i are masked (their moments and caps select to zero, so
+// an exponential that overflowed never reaches a result), segment k counts only
+// when 1 <= k <= i, and key 0 and key i get half caps.
+template <bool kBF16, bool kEdge>
+__device__ __forceinline__ void fwd_chunk_perm(const uint32_t* raw, float2 scale2, float2 nm2, int kc, int i,
+                                               float& sa, float& ea, float& bprev, float2& z2, uint32_t t_p) {
+  const float2 l2e = splat2(kLog2e);
+  float2 sv[8], ev[8], nd[8], rn[8], ps[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    sv[j] = mul2(make_float2(__uint_as_float(raw[2 * j]), __uint_as_float(raw[2 * j + 1])), scale2);
+  // the special-function work (two exponentials, two reciprocals per pair) interleaved
+  // with the series polynomial, which needs only the score differences
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 arg = fma2(sv[j], l2e, nm2);
+    nd[j] = sub2(j ? sv[j - 1] : make_float2(sa, sv[7].x), sv[j]);        // a - b = -d
+    ev[j] = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+    rn[j] = make_float2(rcp_approx(nd[j].x), rcp_approx(nd[j].y));        // -1/d
+    float2 p = fma2(splat2(-1.f / 30.f), nd[j], splat2(1.f / 8.f));      // J1 series in -nd
+    p = fma2(p, nd[j], splat2(-1.f / 3.f));
+    ps[j] = fma2(p, nd[j], splat2(1.f / 2.f));
+  }
+  float2 M1[8], W[8], za = splat2(0.f), zb = splat2(0.f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 eL = j ? ev[j - 1] : make_float2(ea, ev[7].x);
+    const float2 m0c = mul2(sub2(eL, ev[j]), rn[j]);                     // (Eb - Ea) / d
+    const float2 m1c = mul2(sub2(m0c, ev[j]), rn[j]);                    // (Eb - M0) / d
+    float2 m1 = make_float2(sel_series(m1c.x, nd[j].x, eL.x, ps[j].x, kSeriesMaxFwd),
+                            sel_series(m1c.y, nd[j].y, eL.y, ps[j].y, kSeriesMaxFwd));
+    float2 m0 = fma2(nd[j], m1, ev[j]);                                   // Eb - d M1
+    if (kEdge) {
+      const int kx = kc + j, ky = kc + j + 8;                            // right keys of the two segments
+      const bool okx = kx >= 1 && kx <= i, oky = ky <= i;
+      m1 = make_float2(okx ? m1.x : 0.f, oky ? m1.y : 0.f);
+      m0 = make_float2(okx ? m0.x : 0.f, oky ? m0.y : 0.f);
+    }
+    M1[j] = m1;
+    float2 w = sub2(m0, m1);                                             // A of the segment
+    if (j & 1) zb = add2(zb, m0);
+    else za = add2(za, m0);
+    if (kEdge) {
+      // slots j, j+8 hold keys kc-1+j, kc+7+j: half caps on key 0 and key i
+      const int wx = kc - 1 + j, wy = kc + 7 + j;
+      const float nx = (wx == 0 ? 1.f : 0.f) + (wx == i ? 1.f : 0.f);
+      const float ny = (wy == i ? 1.f : 0.f);
+      const float2 cap = make_float2(nx > 0.f ? 0.5f * nx * eL.x : 0.f, ny > 0.f ? 0.5f * eL.y : 0.f);
+      w = add2(w, cap);
+      za = add2(za, cap);
+    }
+    W[j] = w;
+  }
+  z2 = add2(z2, add2(za, zb));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) W[j] = add2(W[j], j ? M1[j - 1] : make_float2(bprev, M1[7].x));
+  bprev = M1[7].y;
+  sa = sv[7].y;
+  ea = ev[7].y;
+  // natural order: TMEM column m of each half holds slots (2m, 2m+1)
+  uint32_t hi[8], lo[8];
+  if (kBF16) {
+    // hi = the upper 16 bits of each weight (bf16 by truncation), lo = the exact fp32
+    // remainder rounded to bf16: ~16 significant bits per weight
+    float2 rz[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 tr = make_float2(__uint_as_float(__float_as_uint(W[j].x) & 0xffff0000u),
+                                    __uint_as_float(__float_as_uint(W[j].y) & 0xffff0000u));
+      rz[j] = sub2(W[j], tr);
+    }
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const float a = m < 4 ? W[2 * m].x : W[2 * m - 8].y, b = m < 4 ? W[2 * m + 1].x : W[2 * m - 7].y;
+      const float ra = m < 4 ? rz[2 * m].x : rz[2 * m - 8].y, rb = m < 4 ? rz[2 * m + 1].x : rz[2 * m - 7].y;
+      hi[m] = __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+      lo[m] = pack_bf16x2(ra, rb);
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const float a = m < 4 ? W[2 * m].x : W[2 * m - 8].y, b = m < 4 ? W[2 * m + 1].x : W[2 * m - 7].y;
+      const uint32_t h2 = pack_f16x2(a, b);
+      const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
+      hi[m] = h2;
+      lo[m] = pack_f16x2(a - __low2float(hh), b - __high2float(hh));
+    }
+  }
+  tmem_st8(t_p, hi);
+  tmem_st8(t_p + 8, lo);
+}
+
+// Half-tile row max over the visible keys of 64 raw scores in permuted order
+// (column 16c+2j+s = key kb+16c+j+8s): a tree of three-input maxima.
+template <bool kDiag>
+__device__ __forceinline__ float perm_max64(const uint32_t (&a)[32], const uint32_t (&b)[32], int kb, int i) {
+  float v[64];
+#pragma unroll
+  for (int x = 0; x < 64; ++x) {
+    const float f = __uint_as_float(x < 32 ? a[x] : b[x - 32]);
+    if (kDiag) {
+      const int key = kb + 16 * (x >> 4) + ((x & 15) >> 1) + 8 * (x & 1);
+      v[x] = key <= i ? f : -INFINITY;
+    } else {
+      v[x] = f;
+    }
+  }
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    m[k] = max3f(v[8 * k], v[8 * k + 1], v[8 * k + 2]);
+    m[k] = max3f(m[k], v[8 * k + 3], v[8 * k + 4]);
+    m[k] = max3f(m[k], v[8 * k + 5], v[8 * k + 6]);
+    m[k] = fmaxf(m[k], v[8 * k + 7]);
+  }
+  return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+template <bool kBF16>
+__device__ void math_warps_perm(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32,
+                                float* stats, int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d,
+                                int H, int o_bthd) {
+  volatile int* ab = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = warp * 32 + lane;
+  const int i = q0 + r;
+  const bool row_ok = i < Tn;
+  const float scale = expf(log_gain[h]) * inv_sqrt_d;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t tO = tmem + TMEM_O + lane_base;
+
+  float m_used = -INFINITY, bpend = 0.f, sprev = 0.f;
+  float2 z2 = splat2(0.f);
+  const float2 scale2 = splat2(scale);
+  bool ok = true;
+  for (int hh = 0; hh < nh; ++hh) {
+    const int reg = hh % NREG;
+    const bool got = mbar_wait(&sm.bar_s_full[reg], (hh / NREG) & 1, ab);
+    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+    tc_fence_after();
+    const uint32_t tS = tmem + HB * reg + lane_base;
+    const int kb = hh * HB;
+    const bool diag = hh >= nh - 2;
+    float tmax;
+    {
+      uint32_t sa_[32], sb_[32];
+      tmem_ld32(tS, sa_);
+      tmem_ld32(tS + 32, sb_);
+      tmem_ld_wait();
+      tmem_reg_fence(sa_);
+      tmem_reg_fence(sb_);
+      tmax = diag ? perm_max64<true>(sa_, sb_, kb, i) : perm_max64<false>(sa_, sb_, kb, i);
+    }
+    tmax *= scale;
+    const bool need = tmax > m_used + kRescaleNats;
+    if (hh == 0) {
+      m_used = tmax;
+    } else if (__any_sync(0xffffffffu, need)) {
+      // as in math_warps: wait for the last P V' before touching O
+      const bool got2 = mbar_wait(&sm.bar_pv_done[(hh - 1) & 1], ((hh - 1) >> 1) & 1, ab);
+      if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
+      tc_fence_after();
+      const float m_new = need ? tmax : m_used;
+      const float alpha = exp_rel(m_used - m_new);
+      z2 = mul2(z2, splat2(alpha));
+      bpend *= alpha;
+      m_used = m_new;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ov[32];
+        tmem_ld32(tO + 32 * half, ov);
+        tmem_ld_wait();
+        tmem_reg_fence(ov);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) ov[x] = __float_as_uint(__uint_as_float(ov[x]) * alpha);
+        tmem_st32(tO + 32 * half, ov);
+      }
+      tmem_st_wait();
+    }
+    const float m2 = m_used * kLog2e;
+    const float2 nm2 = splat2(-m2);
+    float sa = sprev;
+    float ea = (kb > 0) ? ex2_approx(fmaf(sprev, kLog2e, -m2)) : 0.f;
+    float bprev = bpend;
+    // P, 16 keys at a time; the next chunk's TMEM load overlaps this chunk's math
+    uint32_t bufA[16], bufB[16];
+    tmem_ld16(tS, bufA);
+    tmem_ld_wait();
+    tmem_reg_fence(bufA);
+    if (!diag && kb > 0) {
+      // every key of the half-tile is visible to every row of the CTA, no caps
+#pragma unroll 1
+      for (int ch = 0; ch < HB / 16; ch += 2) {
+        tmem_ld16(tS + 16 * (ch + 1), bufB);
+        fwd_chunk_perm<kBF16, false>(bufA, scale2, nm2, kb + 16 * ch, i, sa, ea, bprev, z2, tS + 16 * ch);
+        tmem_ld_wait();
+        tmem_reg_fence(bufB);
+        if (ch + 2 < HB / 16) tmem_ld16(tS + 16 * (ch + 2), bufA);
+        fwd_chunk_perm<kBF16, false>(bufB, scale2, nm2, kb + 16 * (ch + 1), i, sa, ea, bprev, z2,
+                                     tS + 16 * (ch + 1));
+        tmem_ld_wait();
+        tmem_reg_fence(bufA);
+      }
+    } else {
+#define CA_FWD_PCHUNK(BUF, CH)                                                                                \
+  {                                                                                                         \
+    const int kind = fwd_chunk_kind(CH, kb, q0, warp, diag);                                                \
+    if (kind == 1) fwd_chunk_perm<kBF16, false>(BUF, scale2, nm2, kb + 16 * (CH), i, sa, ea, bprev, z2,      \
+                                                tS + 16 * (CH));                                            \
+    else if (kind == 2) fwd_chunk_perm<kBF16, true>(BUF, scale2, nm2, kb + 16 * (CH), i, sa, ea, bprev, z2,  \
+                                                    tS + 16 * (CH));                                        \
+    else fwd_chunk_zero(CH, ea, bprev, tS);                                                                 \
+  }
+#pragma unroll 1
+      for (int ch = 0; ch < HB / 16; ch += 2) {
+        tmem_ld16(tS + 16 * (ch + 1), bufB);
+        CA_FWD_PCHUNK(bufA, ch);
+        tmem_ld_wait();
+        tmem_reg_fence(bufB);
+        if (ch + 2 < HB / 16) tmem_ld16(tS + 16 * (ch + 2), bufA);
+        CA_FWD_PCHUNK(bufB, ch + 1);
+        tmem_ld_wait();
+        tmem_reg_fence(bufA);
+      }
+#undef CA_FWD_PCHUNK
+    }
+    if (hh == nh - 1 && i == kb + HB - 1) {   // key i is the last key: its cap stays pending
+      bprev += 0.5f * ea;
+      z2.x += 0.5f * ea;
+    }
+    bpend = bprev;
+    sprev = sa;
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(&sm.bar_p_ready[reg]);
+  }
+
+  if (ok) ok = mbar_wait(&sm.bar_o_done, 0, ab);
+  tc_fence_after();
+  uint32_t oa[2][32];
+  tmem_ld32(tO, oa[0]);
+  tmem_ld32(tO + 32, oa[1]);
+  tmem_ld_wait();
+  tmem_reg_fence(oa[0]);
+  tmem_reg_fence(oa[1]);
+  if (!ok || !row_ok) return;
+  float acc[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) acc[d] = __uint_as_float(oa[d / 32][d % 32]);
+  const size_t row = (size_t)bh * Tn + i;
+  if (bpend != 0.f) {
+    const uint16_t* vr = reinterpret_cast<const uint16_t*>(vptr) + row * HD;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) {
+      const uint32_t bits = (uint32_t)vr[d];
+      float vv;
+      if (kBF16) vv = __uint_as_float(bits << 16);
+      else vv = __half2float(__ushort_as_half((unsigned short)bits));
+      acc[d] = fmaf(bpend, vv, acc[d]);
+    }
+  }
+  const float z = z2.x + z2.y;
+  const float inv = 1.f / z;
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + act_row(row, Tn, H, o_bthd) * HD);
+#pragma unroll
+  for (int c = 0; c < HD / 8; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a0 = acc[8 * c + 2 * u] * inv, a1 = acc[8 * c + 2 * u + 1] * inv;
+      w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+    }
+    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (o32) {
+    float4* d32 = reinterpret_cast<float4*>(o32 + row * HD);
+#pragma unroll
+    for (int c = 0; c < HD / 4; ++c)
+      d32[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
+  }
+  if (stats) {
+    stats[2 * row] = m_used;
+    stats[2 * row + 1] = z;
+  }
 }
 
 template <bool kBF16>
@@ -483,7 +794,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   }
 }
 
-template <bool kBF16>
+template <bool kBF16, bool kPerm>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
 fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const void* __restrict__ vptr,
@@ -533,8 +844,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   pdl_launch_dependents();
 
   if (warp == 4) {
-    producer<kBF16>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
+    producer<kBF16, kPerm>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
     __syncwarp();
+  } else if (kPerm) {
+    math_warps_perm<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H,
+                           o_bthd);
   } else {
     math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H, o_bthd);
   }
@@ -881,17 +1195,23 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
 // scale*dS and P for 8 consecutive keys of one query row, packed as 16-bit pairs.
 // The exponentials are taken against m + ln Z (E = e^{s-m}/Z), so every moment,
 // and with it P and dS, comes out normalised; g = (dP - D) * scale, so the
-// result is the scale*dS the dK/dQ products need.  On entry (sc, ec, gc) belong
-// to the current key (kfirst) and (Rprev, Bprev) are the right shares of the
-// segment into it; sv/pv[off .. off+7] hold the raw scores / dP of keys
-// kfirst .. kfirst+7 (entry off is the current key) and the next key's come
+// result is the scale*dS the dK/dQ products need.
+// The analytic VJP (analytic_reference.py:52-75) gives key c, between segments
+// c (key c-1 -> c) and c+1, the score gradient
+//   dS_c = g_{c-1} (M1-M2)_c + g_c M2_c + g_c (M0-M1)_{c+1} + g_{c+1} (M1-M2)_{c+1} + cap_c g_c,
+// and with P_c = M1_c + (M0-M1)_{c+1} + cap_c and H_k = (g_k - g_{k-1}) (M1-M2)_k
+// that is  dS_c = g_c P_c + H_{c+1} - H_c:  per segment one product H, per key one
+// fused multiply-add, the caps included through P.
+// On entry (sc, ec, gc) belong to the current key (kfirst) and (Hprev, Bprev) are
+// H and M1 of the segment into it; sv/pv[off .. off+7] hold the raw scores / dP of
+// keys kfirst .. kfirst+7 (entry off is the current key) and the next key's come
 // from sv/pv[off+8] or, past the end, from s_next / p_next.  gsum collects
 // scale * sum dS*s.  kEdge handles masking and caps.
 template <bool kBF16, bool kEdge>
 __device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32_t (&pv)[16], int off,
                                           uint32_t s_next, uint32_t p_next, int kfirst, int i, bool row_ok,
                                           float scale, float m2, float dds, float& sc, float& ec, float& gc,
-                                          float& Rprev, float& Bprev, float& gsum, uint32_t (&pk)[4],
+                                          float& Hprev, float& Bprev, float& gsum, uint32_t (&pk)[4],
                                           uint32_t (&dk)[4]) {
 #pragma unroll
   for (int x = 0; x < 8; x += 2) {
@@ -919,25 +1239,24 @@ __device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32
         M1 = vn ? M1 : 0.f;
         M2 = vn ? M2 : 0.f;
       }
-      const float G = gn - gc;
       const float Anext = M0 - M1;
-      const float GM2 = G * M2;
-      const float Lnext = fmaf(gc, Anext, fmaf(G, M1, -GM2));   // g_c (M0-M1) + G (M1-M2)
-      const float Rn = fmaf(gc, M1, GM2);                       // g_c M1 + G M2
+      const float Hn = (gn - gc) * (M1 - M2);
       float ds, p;
       if (kEdge) {
         const bool vc = row_ok && key >= 0 && key <= i;
-        const float cap = 0.5f * ec * ((key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f));
-        ds = vc ? fmaf(cap, gc, Rprev + Lnext) : 0.f;
-        p = vc ? Bprev + Anext + cap : 0.f;
+        const float nc = (key == 0 ? 1.f : 0.f) + (key == i ? 1.f : 0.f);
+        p = Bprev + Anext + (nc > 0.f ? 0.5f * nc * ec : 0.f);
+        ds = fmaf(gc, p, Hn - Hprev);
+        ds = vc ? ds : 0.f;
+        p = vc ? p : 0.f;
       } else {
-        ds = Rprev + Lnext;
         p = Bprev + Anext;
+        ds = fmaf(gc, p, Hn - Hprev);
       }
       gsum = fmaf(ds, sc, gsum);
       po[u] = p;
       dso[u] = ds;
-      Rprev = Rn;
+      Hprev = Hn;
       Bprev = M1;
       sc = sn;
       ec = en;
@@ -953,14 +1272,15 @@ __device__ __forceinline__ void bwd_keys8(const uint32_t (&sv)[16], const uint32
 // keys (2x, 2x+1) form the natural register pairs of the raw TMEM rows, so s,
 // g and the exponent argument are computed packed there; each exponential goes
 // straight into the right-key pair (2x+1, 2x+2) where the moment recurrences use
-// it.  Products that mix the two layouts (differences, Ea * series, the final
-// L/R and A/B sums) are scalar.  The moments match seg_moments012_sel bit for
-// bit; L is formed as g_c A + G (M1 - M2).  ec carries e of key 0 between calls
-// (sc, gc are recomputed from the raw row); gsum2 collects scale * dS * s.
+// it.  Products that mix the two layouts (differences, the final sums with the
+// previous segment's H and M1) are scalar.  The moments match seg_moments012_sel
+// bit for bit; dS = g P + H_next - H as in bwd_keys8.  ec carries e of key 0
+// between calls (sc, gc are recomputed from the raw row); gsum2 collects
+// scale * dS * s.
 template <bool kBF16>
 __device__ __forceinline__ void bwd_keys8_fast(const uint32_t (&sv)[16], const uint32_t (&pv)[16], int off,
                                                uint32_t s_next, uint32_t p_next, float scale, float m2, float dds,
-                                               float& ec, float& Rprev, float& Bprev, float2& gsum2,
+                                               float& ec, float& Hprev, float& Bprev, float2& gsum2,
                                                uint32_t (&pk)[4], uint32_t (&dk)[4]) {
   const float2 scale2 = splat2(scale), l2e = splat2(kLog2e), nm2 = splat2(-m2), ndds = splat2(-dds);
   const float2 neg1 = splat2(-1.f), neg2 = splat2(-2.f), half = splat2(0.5f);
@@ -998,19 +1318,17 @@ __device__ __forceinline__ void bwd_keys8_fast(const uint32_t (&sv)[16], const u
     float2 ser = fma2(splat2(-1.f / 36.f), nd, splat2(1.f / 10.f));
     ser = fma2(ser, nd, splat2(-1.f / 4.f));
     ser = fma2(ser, nd, splat2(1.f / 3.f));
-    float2 M2;
-    M2.x = fabsf(nd.x) < kSeriesMaxBwd ? e[2 * x] * ser.x : m2c.x;
-    M2.y = fabsf(nd.y) < kSeriesMaxBwd ? e[2 * x + 1] * ser.y : m2c.y;
+    const float2 M2 = make_float2(sel_series(m2c.x, nd.x, e[2 * x], ser.x, kSeriesMaxBwd),
+                                  sel_series(m2c.y, nd.y, e[2 * x + 1], ser.y, kSeriesMaxBwd));
     const float2 M1 = mul2(fma2(nd, M2, EB), half);
     const float2 M0 = fma2(nd, M1, EB);
-    const float2 A = fma2(M1, neg1, M0);
-    const float2 G = make_float2(gA[x].y - gA[x].x, gBy - gA[x].y);
-    const float2 L = fma2(gA[x], A, mul2(G, fma2(M2, neg1, M1)));
-    const float2 R = fma2(gA[x], M1, mul2(G, M2));
-    const float ds0 = Rprev + L.x, ds1 = R.x + L.y;
+    const float2 A = sub2(M0, M1);
+    const float2 H = mul2(make_float2(gA[x].y - gA[x].x, gBy - gA[x].y), sub2(M1, M2));
     const float p0 = Bprev + A.x, p1 = M1.x + A.y;
-    gsum2 = fma2(make_float2(ds0, ds1), sA[x], gsum2);
-    Rprev = R.y;
+    const float2 DS = fma2(gA[x], make_float2(p0, p1), make_float2(H.x - Hprev, H.y - H.x));
+    const float ds0 = DS.x, ds1 = DS.y;
+    gsum2 = fma2(DS, sA[x], gsum2);
+    Hprev = H.y;
     Bprev = M1.y;
     pk[x] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
     dk[x] = kBF16 ? pack_bf16x2(ds0, ds1) : pack_f16x2(ds0, ds1);
@@ -1088,77 +1406,92 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     // its rows (i0+32rq .. i0+32rq+31), inside [0, T) and capless: no masking needed
     const int kbase = j0 + 32 * qk;              // key of local column 0
     const bool interior = kbase >= 1 && kbase + 32 <= i0 + 32 * rq && i0 + 32 * rq + 32 <= Tn;
-    // chunk 0: left halo, keys 0..15, key 16
-    uint32_t s_lo, p_lo, s16, p16, sv[16], pv[16];
-    tmem_ld1(colS - 1, s_lo);
-    tmem_ld16(colS, sv);
-    tmem_ld1(colS + 16, s16);
-    tmem_ld1(colP - 1, p_lo);
-    tmem_ld16(colP, pv);
-    tmem_ld1(colP + 16, p16);
-    tmem_ld_wait();
-    tmem_reg_fence(s_lo);
-    tmem_reg_fence(sv);
-    tmem_reg_fence(s16);
-    tmem_reg_fence(p_lo);
-    tmem_reg_fence(pv);
-    tmem_reg_fence(p16);
-    // the segment from the left halo key into key kbase
-    float sa = __uint_as_float(s_lo) * scale;
-    float ga = fmaf(__uint_as_float(p_lo), scale, -dds);
-    float sc = __uint_as_float(sv[0]) * scale;
-    float gc = fmaf(__uint_as_float(pv[0]), scale, -dds);
-    float ea, ec, Rprev, Bprev;
-    {
-      const bool va = interior || (row_ok && kbase - 1 >= 0 && kbase - 1 <= i);
-      const bool vc = interior || (row_ok && kbase <= i);
-      ea = va ? ex2_approx(fmaf(sa, kLog2e, -m2)) : 0.f;
-      ec = vc ? ex2_approx(fmaf(sc, kLog2e, -m2)) : 0.f;
-      float M0, M1, M2;
-      seg_moments012_sel(ea, ec, sc - sa, M0, M1, M2);
-      const bool ok0 = vc && kbase >= 1;
-      const float G = gc - ga;
-      Rprev = ok0 ? fmaf(ga, M1, G * M2) : 0.f;
-      Bprev = ok0 ? M1 : 0.f;
-    }
     uint8_t* const prow = pbuf + (uint32_t)r * 128;
     uint8_t* const drow = dbuf + (uint32_t)r * 128;
     const int swz = r & 7;
-    uint32_t pk[4], dk[4];
+    // only on the diagonal tile: every key of this quarter lies beyond every row of
+    // the warp, so its P and dS are zero (its left neighbour quarter reads the
+    // halo key from TMEM itself)
+    const bool dead = kbase > i0 + 32 * rq + 31;
+    if (dead) {
+      tc_fence_before();
+      mbar_arrive(&sm.bar_s_consumed);
+      if (t > 0) {
+        const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
+        if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
+      }
+      const uint32_t zz[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) store_chunk(prow, drow, chunk0 + c, swz, zz, zz);
+    } else {
+      // chunk 0: left halo, keys 0..15, key 16
+      uint32_t s_lo, p_lo, s16, p16, sv[16], pv[16];
+      tmem_ld1(colS - 1, s_lo);
+      tmem_ld16(colS, sv);
+      tmem_ld1(colS + 16, s16);
+      tmem_ld1(colP - 1, p_lo);
+      tmem_ld16(colP, pv);
+      tmem_ld1(colP + 16, p16);
+      tmem_ld_wait();
+      tmem_reg_fence(s_lo);
+      tmem_reg_fence(sv);
+      tmem_reg_fence(s16);
+      tmem_reg_fence(p_lo);
+      tmem_reg_fence(pv);
+      tmem_reg_fence(p16);
+      // the segment from the left halo key into key kbase
+      float sa = __uint_as_float(s_lo) * scale;
+      float ga = fmaf(__uint_as_float(p_lo), scale, -dds);
+      float sc = __uint_as_float(sv[0]) * scale;
+      float gc = fmaf(__uint_as_float(pv[0]), scale, -dds);
+      float ea, ec, Hprev, Bprev;
+      {
+        const bool va = interior || (row_ok && kbase - 1 >= 0 && kbase - 1 <= i);
+        const bool vc = interior || (row_ok && kbase <= i);
+        ea = va ? ex2_approx(fmaf(sa, kLog2e, -m2)) : 0.f;
+        ec = vc ? ex2_approx(fmaf(sc, kLog2e, -m2)) : 0.f;
+        float M0, M1, M2;
+        seg_moments012_sel(ea, ec, sc - sa, M0, M1, M2);
+        const bool ok0 = vc && kbase >= 1;
+        Hprev = ok0 ? (gc - ga) * (M1 - M2) : 0.f;
+        Bprev = ok0 ? M1 : 0.f;
+      }
+      uint32_t pk[4], dk[4];
 #define CA_KEYS8(EDGE, OFF, SN, PN, KF)                                                                   \
-  bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Rprev, Bprev, gsum, pk, dk)
+    bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Hprev, Bprev, gsum, pk, dk)
 #define CA_KEYS8_ANY(OFF, SN, PN, KF)                                                                     \
-  if (interior) bwd_keys8_fast<kBF16>(sv, pv, OFF, SN, PN, scale, m2, dds, ec, Rprev, Bprev, gsum2, pk, dk); \
-  else CA_KEYS8(true, OFF, SN, PN, KF);
-    // keys 0..7 are computed before waiting for the previous tile's dV/dK/dQ products,
-    // which still read the shared P/dS buffer; their latency hides behind this work
-    CA_KEYS8_ANY(0, s16, p16, kbase);
-    if (t > 0) {
-      const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
-      if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
-    }
-    store_chunk(prow, drow, chunk0, swz, pk, dk);
-    CA_KEYS8_ANY(8, s16, p16, kbase + 8);
-    store_chunk(prow, drow, chunk0 + 1, swz, pk, dk);
-    // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
-    uint32_t s_hi, p_hi;
-    tmem_ld16(colS + 16, sv);
-    tmem_ld1(colS + 32, s_hi);
-    tmem_ld16(colP + 16, pv);
-    tmem_ld1(colP + 32, p_hi);
-    tmem_ld_wait();
-    tmem_reg_fence(sv);
-    tmem_reg_fence(s_hi);
-    tmem_reg_fence(pv);
-    tmem_reg_fence(p_hi);
-    tc_fence_before();
-    mbar_arrive(&sm.bar_s_consumed);
-    CA_KEYS8_ANY(0, s_hi, p_hi, kbase + 16);
-    store_chunk(prow, drow, chunk0 + 2, swz, pk, dk);
-    CA_KEYS8_ANY(8, s_hi, p_hi, kbase + 24);
-    store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
+    if (interior) bwd_keys8_fast<kBF16>(sv, pv, OFF, SN, PN, scale, m2, dds, ec, Hprev, Bprev, gsum2, pk, dk); \
+    else CA_KEYS8(true, OFF, SN, PN, KF);
+      // keys 0..7 are computed before waiting for the previous tile's dV/dK/dQ products,
+      // which still read the shared P/dS buffer; their latency hides behind this work
+      CA_KEYS8_ANY(0, s16, p16, kbase);
+      if (t > 0) {
+        const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
+        if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
+      }
+      store_chunk(prow, drow, chunk0, swz, pk, dk);
+      CA_KEYS8_ANY(8, s16, p16, kbase + 8);
+      store_chunk(prow, drow, chunk0 + 1, swz, pk, dk);
+      // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
+      uint32_t s_hi, p_hi;
+      tmem_ld16(colS + 16, sv);
+      tmem_ld1(colS + 32, s_hi);
+      tmem_ld16(colP + 16, pv);
+      tmem_ld1(colP + 32, p_hi);
+      tmem_ld_wait();
+      tmem_reg_fence(sv);
+      tmem_reg_fence(s_hi);
+      tmem_reg_fence(pv);
+      tmem_reg_fence(p_hi);
+      tc_fence_before();
+      mbar_arrive(&sm.bar_s_consumed);
+      CA_KEYS8_ANY(0, s_hi, p_hi, kbase + 16);
+      store_chunk(prow, drow, chunk0 + 2, swz, pk, dk);
+      CA_KEYS8_ANY(8, s_hi, p_hi, kbase + 24);
+      store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
 #undef CA_KEYS8_ANY
 #undef CA_KEYS8
+    }
     // dQ of the previous query tile: TMEM -> swizzled f32 staging tile, which the
     // producer adds into the global accumulator with two TMA reduces once every
     // warp has arrived on p_ready.  The staging tile is free once the reduce of
@@ -1361,6 +1694,24 @@ static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T
   return r == CUDA_SUCCESS;
 }
 
+// [BH, T, D] 16-bit tensor (D = 64, T a multiple of 16) viewed as (D, s, j, chunk, BH) with
+// row = 16 chunk + j + 8 s, box = {64, 2, 8, box_rows/16, 1}: a box lands in shared memory
+// with key 16c+j+8s of its c-th 16-row chunk in row 16c+2j+s (128-byte swizzle, OOB -> 0)
+static bool make_map_perm(CUtensorMap* m, const void* base, long long BH, long long T, bool bf16,
+                          unsigned box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || T % 16 != 0 || box_rows % 16 != 0) return false;
+  cuuint64_t dims[5] = {64, 2, 8, (cuuint64_t)(T / 16), (cuuint64_t)BH};
+  cuuint64_t strides[4] = {8 * 128, 128, 16 * 128, (cuuint64_t)(T * 128)};
+  cuuint32_t box[5] = {64, 2, 8, box_rows / 16, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // [B, T, H, D] 16-bit tensor viewed as (D, H, T, B), box = {64 (D), 1, box_rows, 1}: for
 // one (b, h) the same box_rows rows of 128 bytes as make_map's box, 128-byte swizzle, OOB -> 0
 static bool make_map_bthd(CUtensorMap* m, const void* base, long long B, long long H, long long T, long long D,
@@ -1396,6 +1747,17 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 static int num_sms() { return num_sms_cached(); }
 
+// CA_B200_NO_PERM=1 in the environment selects the unpermuted kernels for every T
+// (a comparison switch for tests; read once).
+static bool perm_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("CA_B200_NO_PERM");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 bool forward_supported(const FwdArgs& a) {
   return (a.dtype == 1 || a.dtype == 2) && a.D == 64 && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) &&
          aligned16(a.o) && (!a.o_f32 || aligned16(a.o_f32)) && encode_fn() != nullptr;
@@ -1407,14 +1769,18 @@ bool backward_supported(const BwdArgs& a) {
 int forward_launches(const FwdArgs&) { return 1; }
 int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ cast (+ d log_gain)
 
+// The permuted-key kernels need T a multiple of 16 (whole 16-key chunks in the 5-D view).
+static bool perm_layout(long long T) { return T % 16 == 0 && !perm_disabled(); }
+
 template <bool kBF16>
 static cudaError_t launch_fwd(const FwdArgs& a) {
   const long long BH = a.B * a.H;
+  const bool perm = perm_layout(a.T);
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, fwd::BM) || !make_map(&mk, a.k, BH, a.T, a.D, kBF16, fwd::HB) ||
-      !make_map(&mv, a.v, BH, a.T, a.D, kBF16, fwd::HB))
+  const bool k_ok = perm ? make_map_perm(&mk, a.k, BH, a.T, kBF16, fwd::HB) : make_map(&mk, a.k, BH, a.T, a.D, kBF16, fwd::HB);
+  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, fwd::BM) || !k_ok || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, fwd::HB))
     return cudaErrorInvalidValue;
-  auto kern = fwd::fwd_kernel<kBF16>;
+  auto kern = perm ? fwd::fwd_kernel<kBF16, true> : fwd::fwd_kernel<kBF16, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nqt = (a.T + fwd::BM - 1) / fwd::BM;
