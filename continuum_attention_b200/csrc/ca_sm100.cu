@@ -579,7 +579,7 @@ __device__ void math_warps_perm(Smem& sm, const void* vptr, const float* log_gai
     sprev = sa;
     tmem_st_wait();
     tc_fence_before();
-    mbar_arrive(&sm.bar_p_ready[reg]);
+    mbar_arrive_warp(&sm.bar_p_ready[reg]);
   }
 
   if (ok) ok = mbar_wait(&sm.bar_o_done, 0, ab);
@@ -742,7 +742,7 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
     sprev = sa;
     tmem_st_wait();
     tc_fence_before();
-    mbar_arrive(&sm.bar_p_ready[reg]);
+    mbar_arrive_warp(&sm.bar_p_ready[reg]);
   }
 
   if (ok) ok = mbar_wait(&sm.bar_o_done, 0, ab);
@@ -819,7 +819,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       }
       for (int g = 0; g < NREG; ++g) {
         mbar_init(&sm.bar_s_full[g], 1);
-        mbar_init(&sm.bar_p_ready[g], 128);
+        mbar_init(&sm.bar_p_ready[g], 4);   // one arrival per math warp
       }
       mbar_init(&sm.bar_pv_done[0], 1);
       mbar_init(&sm.bar_pv_done[1], 1);
@@ -1415,7 +1415,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     const bool dead = kbase > i0 + 32 * rq + 31;
     if (dead) {
       tc_fence_before();
-      mbar_arrive(&sm.bar_s_consumed);
+      mbar_arrive_warp(&sm.bar_s_consumed);
       if (t > 0) {
         const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
         if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
@@ -1456,22 +1456,24 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
         Hprev = ok0 ? (gc - ga) * (M1 - M2) : 0.f;
         Bprev = ok0 ? M1 : 0.f;
       }
-      uint32_t pk[4], dk[4];
-#define CA_KEYS8(EDGE, OFF, SN, PN, KF)                                                                   \
-    bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Hprev, Bprev, gsum, pk, dk)
-#define CA_KEYS8_ANY(OFF, SN, PN, KF)                                                                     \
-    if (interior) bwd_keys8_fast<kBF16>(sv, pv, OFF, SN, PN, scale, m2, dds, ec, Hprev, Bprev, gsum2, pk, dk); \
-    else CA_KEYS8(true, OFF, SN, PN, KF);
-      // keys 0..7 are computed before waiting for the previous tile's dV/dK/dQ products,
-      // which still read the shared P/dS buffer; their latency hides behind this work
-      CA_KEYS8_ANY(0, s16, p16, kbase);
+      uint32_t pk[4], dk[4], pk1[4], dk1[4];
+#define CA_KEYS8(EDGE, OFF, SN, PN, KF, PK, DK)                                                           \
+    bwd_keys8<kBF16, EDGE>(sv, pv, OFF, SN, PN, KF, i, row_ok, scale, m2, dds, sc, ec, gc, Hprev, Bprev, gsum, PK, DK)
+#define CA_KEYS8_ANY_TO(OFF, SN, PN, KF, PK, DK)                                                          \
+    if (interior) bwd_keys8_fast<kBF16>(sv, pv, OFF, SN, PN, scale, m2, dds, ec, Hprev, Bprev, gsum2, PK, DK); \
+    else CA_KEYS8(true, OFF, SN, PN, KF, PK, DK);
+#define CA_KEYS8_ANY(OFF, SN, PN, KF) CA_KEYS8_ANY_TO(OFF, SN, PN, KF, pk, dk)
+      // keys 0..15 are computed before waiting for the previous tile's dV/dK/dQ products,
+      // which still read the shared P/dS buffer: the 24 gradient MMAs (about 1.2k
+      // tensor-pipe cycles) finish behind this work
+      CA_KEYS8_ANY_TO(0, s16, p16, kbase, pk, dk);
+      CA_KEYS8_ANY_TO(8, s16, p16, kbase + 8, pk1, dk1);
       if (t > 0) {
         const bool got2 = mbar_wait(&sm.bar_mma_done, (g0 + t - 1) & 1, ab);
         if (!__all_sync(0xffffffffu, got2)) { ok = false; break; }
       }
       store_chunk(prow, drow, chunk0, swz, pk, dk);
-      CA_KEYS8_ANY(8, s16, p16, kbase + 8);
-      store_chunk(prow, drow, chunk0 + 1, swz, pk, dk);
+      store_chunk(prow, drow, chunk0 + 1, swz, pk1, dk1);
       // chunk 1: keys 16..31 and the right halo; S/dP in TMEM are free after this load
       uint32_t s_hi, p_hi;
       tmem_ld16(colS + 16, sv);
@@ -1484,12 +1486,13 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
       tmem_reg_fence(pv);
       tmem_reg_fence(p_hi);
       tc_fence_before();
-      mbar_arrive(&sm.bar_s_consumed);
+      mbar_arrive_warp(&sm.bar_s_consumed);
       CA_KEYS8_ANY(0, s_hi, p_hi, kbase + 16);
       store_chunk(prow, drow, chunk0 + 2, swz, pk, dk);
       CA_KEYS8_ANY(8, s_hi, p_hi, kbase + 24);
       store_chunk(prow, drow, chunk0 + 3, swz, pk, dk);
 #undef CA_KEYS8_ANY
+#undef CA_KEYS8_ANY_TO
 #undef CA_KEYS8
     }
     // dQ of the previous query tile: TMEM -> swizzled f32 staging tile, which the
@@ -1509,7 +1512,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     }
     fence_proxy_async_smem();
     tc_fence_before();
-    mbar_arrive(&sm.bar_p_ready);
+    mbar_arrive_warp(&sm.bar_p_ready);
   }
 
   // last dQ tile (staged for the producer's final reduce) and the dK / dV accumulators
@@ -1526,7 +1529,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     if (ok) {
       stage_dq(sm, r, qk, qv);
       fence_proxy_async_smem();
-      mbar_arrive(&sm.bar_p_ready);
+      mbar_arrive_warp(&sm.bar_p_ready);
     }
   }
   {
@@ -1615,8 +1618,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       mbar_init(&sm.bar_kv, 1);
       for (int s = 0; s < QSTAGES; ++s) mbar_init(&sm.bar_qdo[s], 1);
       mbar_init(&sm.bar_s_full, 1);
-      mbar_init(&sm.bar_s_consumed, NUM_MATH_WARPS * 32);
-      mbar_init(&sm.bar_p_ready, NUM_MATH_WARPS * 32);
+      mbar_init(&sm.bar_s_consumed, NUM_MATH_WARPS);   // one arrival per math warp
+      mbar_init(&sm.bar_p_ready, NUM_MATH_WARPS);
       mbar_init(&sm.bar_mma_done, 1);
       mbar_init(&sm.bar_drain, 1);
       mbar_init(&sm.bar_dq_free, 1);

@@ -44,6 +44,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One arrival for the whole calling warp (converged), after each lane's prior
+// writes -- tcgen05 stores and loads it has waited for, shared-memory writes it
+// has fenced -- are ordered before the warp barrier: the barrier counts warps,
+// not threads, so a phase costs one shared-memory atomic per warp.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 // The issue helpers marked "lane 0" below (expect_tx arrival, TMA copies, MMAs,
 // commits) act only in lane 0 of the calling warp: a producer warp runs its
 // whole loop converged, so descriptors and addresses stay warp-uniform, and the
