@@ -16,6 +16,10 @@ Fixtures:
                      (the cases of the reference's GPU preflight)
   operator_small.npz full op (y, dq, dk, dv, dlog_gain) on small shapes
   operator_cfg1.npz  full op at [2,4,256,32] fp32 inputs, seed 0, gain 1
+  decoder_small.npz  the reference ContinuumDecoderLM (cuda/continuum_attention.py:
+                     784-922) on the CPU in float32: state dict, a batch of bytes,
+                     logits, loss and parameter gradients of a 2-layer d_model-128
+                     model with non-zero per-head gains
 """
 from __future__ import annotations
 
@@ -167,17 +171,49 @@ def make_operator_cfg1(arch):
                         dv=dv.float().numpy(), dlog_gain=dg.numpy())
 
 
+DECODER_CFG = dict(vocab_size=256, block_size=64, d_model=128, n_heads=4, n_layers=2, mlp_ratio=2.0,
+                   dropout=0.0, eps=1e-6, rope_theta=10000.0, grad_checkpointing=False, ca_query_tile=16)
+
+
+def make_decoder(cuda_ca):
+    """The reference decoder end to end on the CPU (its attention runs the CPU branch of
+    _CAExactTiled through _ca_reference_weights), float32 as it trains."""
+    torch.manual_seed(2024)
+    cfg = cuda_ca.ContinuumDecoderConfig(**DECODER_CFG)
+    model = cuda_ca.ContinuumDecoderLM(cfg)
+    with torch.no_grad():
+        for li, block in enumerate(model.blocks):
+            block.attn.log_qk_gain.copy_(torch.tensor([0.1, -0.2, 0.3, 0.0]) * (li + 1))
+    g = torch.Generator().manual_seed(4048)
+    ids = torch.randint(0, 256, (2, 64), generator=g)
+    out = model(ids, ids)
+    out["loss"].backward()
+    rec = {"ids": ids.numpy(), "logits": out["logits"].detach().numpy(), "loss": out["loss"].detach().numpy()}
+    for name, t in model.state_dict().items():
+        rec["param__" + name] = t.numpy()
+    for name, p in model.named_parameters():
+        rec["grad__" + name] = p.grad.numpy()
+    rec["__config__"] = np.array(sorted(DECODER_CFG.items()), dtype=object).astype(str)
+    np.savez_compressed(os.path.join(HERE, "decoder_small.npz"), **rec)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--reference", required=True, help="root of the reference project")
+    p.add_argument("--only", choices=["decoder"], help="write only this fixture")
     args = p.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     arch, aref, cuda_ca = _import_reference(args.reference)
+    if args.only == "decoder":
+        make_decoder(cuda_ca)
+        print("decoder fixture written to", HERE)
+        return
     make_moments(arch, aref)
     make_weights_square(arch, aref)
     make_weights_tile(cuda_ca)
     make_operator_small(arch)
     make_operator_cfg1(arch)
+    make_decoder(cuda_ca)
     print("golden fixtures written to", HERE)
 
 

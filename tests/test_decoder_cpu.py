@@ -80,3 +80,15 @@ def test_clip_and_step_matches_clip_grad_norm_without_fused_adamw():
     ob.step()
     for pa, pb in zip(a.parameters(), b.parameters()):
         assert torch.equal(pa, pb)
+
+
+def test_matches_reference_decoder_on_cpu():
+    """The reference ContinuumDecoderLM's own logits, loss and gradients (fixture made
+    by tests/golden/make_golden.py), reproduced by this decoder on the CPU with the
+    float64 oracle attention in place of the operator: pins the embedding, rotary
+    convention, norms, residual wiring, untied head and loss."""
+    from decoder_fixture import check, compare, load
+    cfg, state, ids, logits, loss, grads = load()
+    model = ContinuumDecoderLM(cfg, attention_fn=cpu_continuum_attention)
+    model.load_state_dict(state)
+    check(compare(model, ids, logits, loss, grads))
