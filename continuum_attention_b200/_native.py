@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(HERE, "libca_b200.so")
 CA_DTYPE_F32, CA_DTYPE_BF16, CA_DTYPE_F16 = 0, 1, 2
 CA_IMPL_AUTO, CA_IMPL_SIMT, CA_IMPL_TCGEN05 = 0, 1, 2
 CA_LAYOUT_BHTD, CA_LAYOUT_BTHD = 0, 1
+CA_BWD_DETERMINISTIC = 1
 STATUS_NAMES = {0: "CA_OK", 1: "CA_ERR_INVALID_ARGUMENT", 2: "CA_ERR_UNSUPPORTED", 3: "CA_ERR_CUDA",
                 4: "CA_ERR_WORKSPACE", 5: "CA_ERR_DEVICE_TIMEOUT"}
 
@@ -32,6 +33,8 @@ SIGNATURES = {
                            _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_backward_ex": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                               _i64, _i64, _i64, _i64, _int, _int, _int, _vp]),
+    "ca_backward_ex2": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                               _i64, _i64, _i64, _i64, _int, _int, _int, _int, _vp]),
     "ca_backward_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                    _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "ca_device_status": (_int, [_int]),

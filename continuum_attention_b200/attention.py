@@ -86,12 +86,14 @@ def workspace_bytes(B, H, T, D, dtype) -> int:
 
 
 def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="auto", workspace=None,
-                 o_f32=None, layout="bhtd"):
+                 o_f32=None, layout="bhtd", deterministic=False):
     """Run the native backward; returns (dq, dk, dv, dlog_gain float32 [H] or None).
 
     ``o_f32`` (optional) is the forward's fp32 accumulator; it makes the row
     terms D_i = dO_i . O_i exact to fp32 for bf16/f16 inputs.  ``layout="bthd"``:
-    o and do are contiguous [B,T,H,D] tensors.
+    o and do are contiguous [B,T,H,D] tensors.  ``deterministic``: dQ is summed in
+    one fixed order, so all four gradients are bitwise reproducible (tcgen05
+    kernels only; RuntimeError where the CUDA-core kernels would run).
     """
     B, H, T, D = q.shape
     lib = _native.lib()
@@ -101,12 +103,13 @@ def backward_raw(q, k, v, o, do, log_gain_f32, stats, want_dgain=True, impl="aut
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
-        st = lib.ca_backward_ex(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v),
-                                None if o is None else ctypes_ptr(o), None if o_f32 is None else ctypes_ptr(o_f32),
-                                ctypes_ptr(do), ctypes_ptr(log_gain_f32), ctypes_ptr(stats), ctypes_ptr(dq),
-                                ctypes_ptr(dk), ctypes_ptr(dv), None if dg is None else ctypes_ptr(dg),
-                                workspace.data_ptr(), workspace.numel(), B, H, T, D,
-                                _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _LAYOUT_CODE[layout], _stream(q.device))
+        st = lib.ca_backward_ex2(ctypes_ptr(q), ctypes_ptr(k), ctypes_ptr(v),
+                                 None if o is None else ctypes_ptr(o), None if o_f32 is None else ctypes_ptr(o_f32),
+                                 ctypes_ptr(do), ctypes_ptr(log_gain_f32), ctypes_ptr(stats), ctypes_ptr(dq),
+                                 ctypes_ptr(dk), ctypes_ptr(dv), None if dg is None else ctypes_ptr(dg),
+                                 workspace.data_ptr(), workspace.numel(), B, H, T, D,
+                                 _DTYPE_CODE[q.dtype], _IMPL_CODE[impl], _LAYOUT_CODE[layout],
+                                 _native.CA_BWD_DETERMINISTIC if deterministic else 0, _stream(q.device))
     _native.check("ca_backward", st)
     return dq, dk, dv, dg
 
@@ -152,13 +155,48 @@ class ContinuumAttentionFunction(torch.autograd.Function):
         # kernels in that storage order (a copy only when it does not arrive that way)
         g = (g.transpose(1, 2) if ctx.out_layout == "bthd" else g).contiguous()
         # with the fp32 accumulator saved, the dtype-rounded output is not needed
-        dq, dk, dv, dg = backward_raw(q, k, v, None if ctx.lowp else o_saved, g, lg, stats,
-                                      want_dgain=want_dgain, impl=_current_impl(),
-                                      o_f32=o_saved if ctx.lowp else None, layout=ctx.out_layout)
+        args = (q, k, v, None if ctx.lowp else o_saved, g, lg, stats)
+        kw = dict(want_dgain=want_dgain, impl=_current_impl(), o_f32=o_saved if ctx.lowp else None,
+                  layout=ctx.out_layout)
+        det = _deterministic_requested()
+        try:
+            dq, dk, dv, dg = backward_raw(*args, deterministic=det, **kw)
+        except RuntimeError as e:
+            # torch.use_deterministic_algorithms(True, warn_only=True): warn and run the
+            # ordinary backward where no deterministic kernel covers the inputs
+            if not (det and "CA_ERR_UNSUPPORTED" in str(e) and torch.is_deterministic_algorithms_warn_only_enabled()):
+                raise
+            import warnings
+            warnings.warn(f"continuum_attention backward is not deterministic here: {e}")
+            dq, dk, dv, dg = backward_raw(*args, deterministic=False, **kw)
         return dq, dk, dv, (dg.to(ctx.gain_dtype) if dg is not None else None), None, None
 
 
 _impl_override = {"impl": "auto"}
+_det_override = {"on": False}
+
+
+def _deterministic_requested() -> bool:
+    """A bitwise-reproducible backward is asked for: deterministic_backward() or
+    torch.use_deterministic_algorithms(True)."""
+    return _det_override["on"] or torch.are_deterministic_algorithms_enabled()
+
+
+class deterministic_backward:
+    """Context manager: backward passes launched inside sum dQ in one fixed order, so
+    dq, dk, dv and d log_gain are bitwise reproducible (bf16/f16 inputs with D = 64)."""
+
+    def __init__(self, on: bool = True):
+        self.on = bool(on)
+
+    def __enter__(self):
+        self.prev = _det_override["on"]
+        _det_override["on"] = self.on
+        return self
+
+    def __exit__(self, *exc):
+        _det_override["on"] = self.prev
+        return False
 
 
 def _current_impl() -> str:

@@ -46,7 +46,7 @@ constexpr long long kMinKeyTile = 64;  // smallest key tile of any backward kern
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct Layout {
-  size_t rowdot, dq_acc, gain_part, counter, total;
+  size_t rowdot, dq_acc, gain_part, counter, ready, total;
   int nparts;
 };
 
@@ -58,7 +58,8 @@ Layout workspace_layout(long long B, long long H, long long T, long long D) {
   l.dq_acc = align_up(l.rowdot + rows * sizeof(float));
   l.gain_part = align_up(l.dq_acc + rows * (size_t)D * sizeof(float));
   l.counter = align_up(l.gain_part + (size_t)B * H * l.nparts * sizeof(float));
-  l.total = align_up(l.counter + sizeof(unsigned));
+  l.ready = align_up(l.counter + sizeof(unsigned));
+  l.total = align_up(l.ready + (size_t)B * H * l.nparts * sizeof(unsigned));
   return l;
 }
 
@@ -149,11 +150,14 @@ size_t ca_backward_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, in
 static int backward_impl(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
                          const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk,
                          void* dv, float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B,
-                         int64_t H, int64_t T, int64_t D, int dtype, int impl, void* stream, int layout) {
+                         int64_t H, int64_t T, int64_t D, int dtype, int impl, void* stream, int layout,
+                         int flags = 0) {
   int st = check_shape(B, H, T, D, dtype, impl);
   if (st != CA_OK) return st;
   st = check_layout("ca_backward", layout);
   if (st != CA_OK) return st;
+  if (flags & ~CA_BWD_DETERMINISTIC) return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: unknown flags 0x%x", flags);
+  const bool det = (flags & CA_BWD_DETERMINISTIC) != 0;
   cudaStream_t s = (cudaStream_t)stream;
   if (B * H * T == 0) {
     if (dlog_gain && H > 0) {
@@ -172,17 +176,28 @@ static int backward_impl(const void* q, const void* k, const void* v, const void
     return fail(CA_ERR_INVALID_ARGUMENT, "ca_backward: workspace must be %zu-byte aligned", kAlign);
   char* ws = (char*)workspace;
   ca::BwdWorkspace w{(float*)(ws + l.rowdot), (float*)(ws + l.dq_acc), (float*)(ws + l.gain_part),
-                     l.nparts, (unsigned*)(ws + l.counter)};
+                     l.nparts, (unsigned*)(ws + l.counter), (unsigned*)(ws + l.ready), (int)(B * H * l.nparts)};
   ca::BwdArgs a{q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, B, H, T, D, dtype,
-                (float)(1.0 / std::sqrt((double)D)), s, layout};
+                (float)(1.0 / std::sqrt((double)D)), s, layout, det ? 1 : 0};
   cudaError_t e;
   g_last_launches = 0;
+  const bool tc = impl != CA_IMPL_SIMT && ca::sm100::backward_supported(a);
+  if (det && !tc)
+    return fail(CA_ERR_UNSUPPORTED,
+                "ca_backward: a deterministic backward needs the tcgen05 kernels (bf16/f16, D = 64, 16-byte "
+                "aligned buffers); the CUDA-core kernels add dQ with atomics (dtype=%d D=%lld impl=%d)",
+                dtype, (long long)D, impl);
   if (impl == CA_IMPL_SIMT) {
     e = ca::simt::backward(a, w);
     g_last_launches = ca::simt::backward_launches(a);
-  } else if (ca::sm100::backward_supported(a)) {
+  } else if (tc) {
     e = ca::sm100::backward(a, w);
     g_last_launches = ca::sm100::backward_launches(a);
+    if (e != cudaSuccess) {
+      char where[320];
+      snprintf(where, sizeof(where), "ca_backward launch (tcgen05 %s)", ca::sm100::backward_stage());
+      return cuda_fail(e, where);
+    }
   } else if (impl == CA_IMPL_TCGEN05) {
     return fail(CA_ERR_UNSUPPORTED, "ca_backward: tcgen05 kernels do not cover dtype=%d D=%lld", dtype,
                 (long long)D);
@@ -208,6 +223,14 @@ int ca_backward_ex(const void* q, const void* k, const void* v, const void* o, c
                    int64_t T, int64_t D, int dtype, int impl, int layout, void* stream) {
   return backward_impl(q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, workspace,
                        workspace_bytes, B, H, T, D, dtype, impl, stream, layout);
+}
+
+int ca_backward_ex2(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                    const void* d_o, const float* log_gain, const float* row_stats, void* dq, void* dk, void* dv,
+                    float* dlog_gain, void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                    int64_t T, int64_t D, int dtype, int impl, int layout, int flags, void* stream) {
+  return backward_impl(q, k, v, o, o_f32, d_o, log_gain, row_stats, dq, dk, dv, dlog_gain, workspace,
+                       workspace_bytes, B, H, T, D, dtype, impl, stream, layout, flags);
 }
 
 static int check_rope(const char* fn, const void* a, const void* b, const void* c, const void* d,

@@ -41,6 +41,7 @@ struct BwdArgs {
   float inv_sqrt_d;
   cudaStream_t stream;
   int act_bthd;        // o and d_o stored [B,T,H,D] instead of [B,H,T,D] (o_f32 stays [B,H,T,D])
+  int deterministic;   // dQ summed in a fixed order (tcgen05 kernels; bitwise reproducible)
 };
 
 // Carved out of the caller's workspace (ca_capi.cu: workspace_layout).
@@ -50,6 +51,8 @@ struct BwdWorkspace {
   float* gain_part;  // [B*H*nparts] per-(head, key tile) partial sums of dS*s
   int nparts;
   unsigned* counter; // work-item counter of the persistent tcgen05 backward (zeroed by prep)
+  unsigned* ready;   // [B*H*nparts] per (head, query tile): dQ contributions added so far (zeroed by prep)
+  int n_ready;
 };
 
 // Launch with programmatic stream serialisation (the kernel calls pdl_wait()
@@ -76,8 +79,10 @@ inline int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ
 cudaError_t forward(const FwdArgs& a);
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
 // backward helpers shared with the tcgen05 path
-// D_i = dO_i . O_i, dq_acc = 0, *counter = 0 (when counter != nullptr)
-cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter);
+// D_i = dO_i . O_i; dq_acc = 0 (when dq_acc != nullptr); *counter = 0 and ready[0 .. n_ready) = 0
+// (when counter != nullptr)
+cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter, unsigned* ready = nullptr,
+                        int n_ready = 0);
 // fp32 dQ -> dtype, and (when a.dlog_gain) d log_gain from the per-key-tile partials, one launch
 cudaError_t launch_cast_dq(const BwdArgs& a, const float* dq_acc, const float* gain_part, int nparts);
 }  // namespace simt
@@ -90,6 +95,8 @@ int forward_launches(const FwdArgs& a);
 int backward_launches(const BwdArgs& a);
 cudaError_t forward(const FwdArgs& a);
 cudaError_t backward(const BwdArgs& a, const BwdWorkspace& w);
+// which step of the calling thread's last backward() ran last (for error messages)
+const char* backward_stage();
 // one CTA whose bounded mbarrier wait runs out after limit_ns (nothing completes the barrier)
 cudaError_t launch_wait_timeout_selftest(unsigned long long limit_ns, cudaStream_t s);
 }  // namespace sm100

@@ -794,12 +794,13 @@ __global__ void rowdot_kernel(const TO* __restrict__ o, const T* __restrict__ do
 // [B,H,T,D] case carries no index arithmetic.
 template <typename TO, typename T, bool kOB, bool kDB>
 __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ dout, float* __restrict__ rowdot,
-                              float* __restrict__ dq_acc, size_t rows, unsigned* __restrict__ counter, int Tn,
-                              int H) {
+                              float* __restrict__ dq_acc, size_t rows, unsigned* __restrict__ counter,
+                              unsigned* __restrict__ ready, int n_ready, int Tn, int H) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid == 0 && counter) *counter = 0u;   // work-item counter of the persistent backward
+  if (ready && gid < (size_t)n_ready) ready[gid] = 0u;   // ordered-dQ turn counters
   const size_t row = gid >> 4;
   const int part = (int)(gid & 15);
   float s = 0.f;
@@ -826,7 +827,7 @@ __global__ void prep64_kernel(const TO* __restrict__ o, const T* __restrict__ do
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) s = fmaf(ov[u], dv[u], s);
-    *reinterpret_cast<float4*>(dq_acc + base) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (dq_acc) *reinterpret_cast<float4*>(dq_acc + base) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll
   for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -951,11 +952,13 @@ static cudaError_t rowdot_dtype(const BwdArgs& a, float* rowdot) {
 }
 
 template <typename T>
-static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter) {
+static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter, unsigned* ready,
+                              int n_ready) {
   const size_t rows = (size_t)a.B * a.H * a.T;
   const uintptr_t oal = reinterpret_cast<uintptr_t>(a.o_f32 ? (const void*)a.o_f32 : a.o);
   const bool vec = a.D == 64 && (reinterpret_cast<uintptr_t>(a.d_o) & (4 * sizeof(T) - 1)) == 0 &&
                    (a.o_f32 || sizeof(T) == 4 ? (oal & 15) == 0 : true);
+  if (!counter) ready = nullptr;
   if (!vec) {
     cudaError_t e = rowdot_dtype<T>(a, rowdot);
     if (e != cudaSuccess) return e;
@@ -963,25 +966,31 @@ static cudaError_t prep_dtype(const BwdArgs& a, float* rowdot, float* dq_acc, un
       e = cudaMemsetAsync(counter, 0, sizeof(unsigned), a.stream);
       if (e != cudaSuccess) return e;
     }
-    return cudaMemsetAsync(dq_acc, 0, rows * a.D * sizeof(float), a.stream);
+    if (ready && n_ready > 0) {
+      e = cudaMemsetAsync(ready, 0, (size_t)n_ready * sizeof(unsigned), a.stream);
+      if (e != cudaSuccess) return e;
+    }
+    return dq_acc ? cudaMemsetAsync(dq_acc, 0, rows * a.D * sizeof(float), a.stream) : cudaSuccess;
   }
-  const unsigned blocks = (unsigned)((rows * 16 + 255) / 256);
+  const size_t threads = std::max<size_t>(rows * 16, ready ? (size_t)n_ready : 0);
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
   const dim3 g(blocks), b(256);
   if (a.o_f32) {
     auto k = a.act_bthd ? prep64_kernel<float, T, false, true> : prep64_kernel<float, T, false, false>;
     return launch_pdl(k, g, b, 0, a.stream, (const float*)a.o_f32, (const T*)a.d_o, rowdot, dq_acc, rows, counter,
-                      (int)a.T, (int)a.H);
+                      ready, n_ready, (int)a.T, (int)a.H);
   }
   auto k = a.act_bthd ? prep64_kernel<T, T, true, true> : prep64_kernel<T, T, false, false>;
-  return launch_pdl(k, g, b, 0, a.stream, (const T*)a.o, (const T*)a.d_o, rowdot, dq_acc, rows, counter, (int)a.T,
-                    (int)a.H);
+  return launch_pdl(k, g, b, 0, a.stream, (const T*)a.o, (const T*)a.d_o, rowdot, dq_acc, rows, counter, ready,
+                    n_ready, (int)a.T, (int)a.H);
 }
 
-cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter) {
+cudaError_t launch_prep(const BwdArgs& a, float* rowdot, float* dq_acc, unsigned* counter, unsigned* ready,
+                        int n_ready) {
   switch (a.dtype) {
-    case 0: return prep_dtype<float>(a, rowdot, dq_acc, counter);
-    case 1: return prep_dtype<__nv_bfloat16>(a, rowdot, dq_acc, counter);
-    default: return prep_dtype<__half>(a, rowdot, dq_acc, counter);
+    case 0: return prep_dtype<float>(a, rowdot, dq_acc, counter, ready, n_ready);
+    case 1: return prep_dtype<__nv_bfloat16>(a, rowdot, dq_acc, counter, ready, n_ready);
+    default: return prep_dtype<__half>(a, rowdot, dq_acc, counter, ready, n_ready);
   }
 }
 

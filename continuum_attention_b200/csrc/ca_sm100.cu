@@ -32,6 +32,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 
 #include "ca_common.cuh"
@@ -970,9 +971,13 @@ __device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tme
 }
 
 // Work item w (heaviest first): key tile kt = w / BH of head-sequence bh = w % BH,
-// with n = nkt - kt query tiles.
+// with n = nkt - kt query tiles.  Tile t of an item is query tile kt + n - 1 - t:
+// the last query tile first and the diagonal tile last, so that every item reaches
+// a given query tile at the same offset from its start, and the items of a head,
+// started in key-tile order (heaviest first), reach it in key-tile order too.
 struct Item {
   int bh, kt, j0, n;
+  __device__ __forceinline__ int row0(int t) const { return j0 + (n - 1 - t) * BM; }
 };
 __device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
   Item it;
@@ -994,10 +999,14 @@ __device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
 // math warps at this item's last tile, and this item's final dQ reduce waits until
 // the next item's first S/dP is issued: the next item's start overlaps this
 // item's epilogue.
-template <bool kBF16, bool kDOB>
+// kDet: each dQ tile receives its key tiles' contributions in ascending key-tile
+// order -- key tile 0 stores, key tile k adds once ready[bh, query tile] == k, then
+// raises it -- so dQ is the same fp32 sum on every run (and the accumulator needs
+// no zeroing).  Otherwise the contributions are reduce-adds in arrival order.
+template <bool kBF16, bool kDOB, bool kDet>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
                          const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int n_items,
-                         unsigned* counter, uint32_t tmem, int H) {
+                         unsigned* counter, unsigned* ready, uint32_t tmem, int H) {
   volatile int* ab = &sm.abort_flag;
   const int lane = threadIdx.x & 31;
   const uint32_t id_s = make_idesc(BM, KH, kBF16, false, false);
@@ -1025,12 +1034,55 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   };
   auto load_qdo = [&](int st, const Item& it, int t) {
     mbar_arrive_expect_tx(&sm.bar_qdo[st], 2 * QT_BYTES);
-    tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
+    tma_load_3d(sm.q[st], tq, &sm.bar_qdo[st], 0, it.row0(t), it.bh);
     if (kDOB)   // dO stored [B][T][H][D]: map (D, H, T, B)
-      tma_load_4d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.bh % H, it.j0 + t * BM, it.bh / H);
+      tma_load_4d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.bh % H, it.row0(t), it.bh / H);
     else
-      tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.j0 + t * BM, it.bh);
+      tma_load_3d(sm.dout[st], tdo, &sm.bar_qdo[st], 0, it.row0(t), it.bh);
     q_pending[st] = true;
+  };
+  unsigned* ready_pending = nullptr;
+  // Deterministic: once the last dQ tile has reached global memory, hand its query
+  // tile to the next key tile (a release increment of its turn counter).
+  auto release_ready = [&]() {
+    if (kDet && ready_pending) {
+      bulk_wait_group0();
+      fence_proxy_async_global();
+      if (lane == 0) red_release_add_gpu(ready_pending, 1u);
+      __syncwarp();
+      ready_pending = nullptr;
+    }
+  };
+  // the staged dQ tile of tile t of item it (two 32-column halves) into the accumulator
+  auto issue_dq = [&](const Item& it, int t) -> bool {
+    const int row0 = it.row0(t);
+    if (kDet) {
+      release_ready();
+      unsigned* rdy = ready + (size_t)it.bh * nkt + row0 / BM;
+      if (it.kt == 0) {
+        tma_store_3d(tdq, sm.dqs[0], 0, row0, it.bh);
+        tma_store_3d(tdq, sm.dqs[1], 32, row0, it.bh);
+      } else {
+        if (!wait_count(rdy, (unsigned)it.kt, ab)) return false;
+        fence_proxy_async_global();
+        tma_reduce_add_3d(tdq, sm.dqs[0], 0, row0, it.bh);
+        tma_reduce_add_3d(tdq, sm.dqs[1], 32, row0, it.bh);
+      }
+      ready_pending = rdy;
+    } else {
+      tma_reduce_add_3d(tdq, sm.dqs[0], 0, row0, it.bh);
+      tma_reduce_add_3d(tdq, sm.dqs[1], 32, row0, it.bh);
+    }
+    bulk_commit_group();
+    return true;
+  };
+  // the staging tile has been read (and, deterministic, the tile written to global
+  // memory, which the next key tile's turn then follows): free it for the math warps
+  auto dq_done = [&]() {
+    bulk_wait_group_read0();
+    if (lane == 0) mbar_arrive(&sm.bar_dq_free);
+    __syncwarp();
+    release_ready();
   };
   auto publish = [&](int w) {
     if (lane == 0) {
@@ -1072,12 +1124,8 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   auto final_reduce = [&](const Item& pi) -> bool {
     if (!mbar_wait_warp(&sm.bar_p_ready, pr & 1, ab)) return false;
     ++pr;
-    tma_reduce_add_3d(tdq, sm.dqs[0], 0, pi.j0 + (pi.n - 1) * BM, pi.bh);
-    tma_reduce_add_3d(tdq, sm.dqs[1], 32, pi.j0 + (pi.n - 1) * BM, pi.bh);
-    bulk_commit_group();
-    bulk_wait_group_read0();
-    if (lane == 0) mbar_arrive(&sm.bar_dq_free);
-    __syncwarp();
+    if (!issue_dq(pi, pi.n - 1)) return false;
+    dq_done();
     return true;
   };
   bool good = item < n_items;
@@ -1146,12 +1194,8 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
       issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
       mma_commit(&sm.bar_mma_done);
       committed = (int)g;
-      // the math warps staged dQ of query tile t-1 before arriving on p_ready
-      if (t > 0) {
-        tma_reduce_add_3d(tdq, sm.dqs[0], 0, it.j0 + (t - 1) * BM, it.bh);
-        tma_reduce_add_3d(tdq, sm.dqs[1], 32, it.j0 + (t - 1) * BM, it.bh);
-        bulk_commit_group();
-      }
+      // the math warps staged dQ of tile t-1 before arriving on p_ready
+      if (t > 0 && !issue_dq(it, t - 1)) { good = false; break; }
       // every math warp is inside this item (it arrived on this tile's p_ready), so
       // the published slot is free: the next item goes out now, and the math warps
       // find it when they finish this one
@@ -1167,11 +1211,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         }
         load_kv(nx);
       }
-      if (t > 0) {
-        bulk_wait_group_read0();
-        if (lane == 0) mbar_arrive(&sm.bar_dq_free);
-        __syncwarp();
-      }
+      if (t > 0) dq_done();
     }
     if (!good) break;
     pending = true;
@@ -1181,6 +1221,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
     good = item < n_items;
   }
   if (pending && !*ab) final_reduce(prev);   // the loop ended normally: the last item's last dQ tile
+  if (!*ab) release_ready();
   // drain: every copy lands and every MMA completes before shared memory / TMEM go away
   mma_commit(&sm.bar_drain);
   int dummy = 0;
@@ -1378,21 +1419,22 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
   float gsum = 0.f;
   float2 gsum2 = splat2(0.f);   // packed partial of gsum from interior key groups
 
-  // row statistics of the next query tile are loaded one iteration ahead
+  // row statistics of the next query tile are loaded one iteration ahead; tile t is
+  // query tile kt + n_tiles - 1 - t (the last query tile first, the diagonal last)
   float nm = 0.f, nz = 1.f, nd = 0.f;
-  if (j0 + r < Tn) {
-    const size_t ri = (size_t)bh * Tn + j0 + r;
+  if (j0 + (n_tiles - 1) * BM + r < Tn) {
+    const size_t ri = (size_t)bh * Tn + j0 + (n_tiles - 1) * BM + r;
     nm = stats[2 * ri];
     nz = stats[2 * ri + 1];
     nd = rowdot[ri];
   }
   for (int t = 0; t < n_tiles; ++t) {
-    const int i0 = j0 + t * BM;
+    const int i0 = j0 + (n_tiles - 1 - t) * BM;
     const int i = i0 + r;
     const bool row_ok = i < Tn;
     const float m = nm, zrow = nz, dd = nd;
-    if (t + 1 < n_tiles && i + BM < Tn) {
-      const size_t ri = (size_t)bh * Tn + i + BM;
+    if (t + 1 < n_tiles) {   // rows i - BM of the next tile are all inside [0, T)
+      const size_t ri = (size_t)bh * Tn + i - BM;
       nm = stats[2 * ri];
       nz = stats[2 * ri + 1];
       nd = rowdot[ri];
@@ -1598,15 +1640,15 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   }
 }
 
-template <bool kBF16, bool kDOB>
+template <bool kBF16, bool kDOB, bool kDet>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
            const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ log_gain,
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            void* __restrict__ dkp, void* __restrict__ dvp,
-           float* __restrict__ gain_part, unsigned* __restrict__ counter, int BH, int H, int Tn,
-           float inv_sqrt_d) {
+           float* __restrict__ gain_part, unsigned* __restrict__ counter, unsigned* __restrict__ ready, int BH,
+           int H, int Tn, float inv_sqrt_d) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1646,8 +1688,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   pdl_launch_dependents();
 
   if (warp == NUM_MATH_WARPS) {
-    producer<kBF16, kDOB>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, tmem,
-                          H);   // converged
+    producer<kBF16, kDOB, kDet>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, ready, tmem,
+                                H);   // converged
     __syncwarp();
   } else {
     math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, n_items, tmem,
@@ -1681,11 +1723,16 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+thread_local char g_map_error[160] = "";
+
 // [BH, T, D] 16-bit tensor, box = {64 (D), box_rows, 1}, 128-byte swizzle, OOB -> 0
 static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T, long long D, bool bf16,
                      unsigned box_rows = 128) {
   EncodeTiledFn enc = encode_fn();
-  if (!enc) return false;
+  if (!enc) {
+    snprintf(g_map_error, sizeof(g_map_error), "cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(T * D * 2)};
   cuuint32_t box[3] = {64, box_rows, 1};
@@ -1694,8 +1741,12 @@ static bool make_map(CUtensorMap* m, const void* base, long long BH, long long T
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    snprintf(g_map_error, sizeof(g_map_error), "encode %d: base %p dims %lld,%lld,%lld box %u", (int)r, base,
+             (long long)D, (long long)T, (long long)BH, box_rows);
   return r == CUDA_SUCCESS;
 }
+const char* map_error() { return g_map_error; }
 
 // [BH, T, D] 16-bit tensor (D = 64, T a multiple of 16) viewed as (D, s, j, chunk, BH) with
 // row = 16 chunk + j + 8 s, box = {64, 2, 8, box_rows/16, 1}: a box lands in shared memory
@@ -1748,6 +1799,19 @@ static bool make_map_f32(CUtensorMap* m, void* base, long long BH, long long T) 
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The tensor-map encoder is a driver call and needs the device's context current
+// on the calling thread.  A thread that has made no runtime call yet -- torch's
+// autograd thread running a backward whose buffers all come from the caching
+// allocator, for instance -- has none, and the encoder then fails with
+// CUDA_ERROR_INVALID_CONTEXT.  cudaSetDevice on the current device binds its
+// primary context to the thread.
+static cudaError_t bind_context() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return cudaSetDevice(dev);
+}
+
 static int num_sms() { return num_sms_cached(); }
 
 // CA_B200_NO_PERM=1 in the environment selects the unpermuted kernels for every T
@@ -1777,6 +1841,8 @@ static bool perm_layout(long long T) { return T % 16 == 0 && !perm_disabled(); }
 
 template <bool kBF16>
 static cudaError_t launch_fwd(const FwdArgs& a) {
+  cudaError_t ce = bind_context();
+  if (ce != cudaSuccess) return ce;
   const long long BH = a.B * a.H;
   const bool perm = perm_layout(a.T);
   CUtensorMap mq, mk, mv;
@@ -1794,19 +1860,41 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
 
 cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a) : launch_fwd<false>(a); }
 
+thread_local const char* g_bwd_stage = "";
+thread_local char g_bwd_stage_buf[256];
+const char* backward_stage() {
+  snprintf(g_bwd_stage_buf, sizeof(g_bwd_stage_buf), "%s%s%s", g_bwd_stage, g_map_error[0] ? "; " : "", g_map_error);
+  return g_bwd_stage_buf;
+}
+
 template <bool kBF16>
 static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
+  g_bwd_stage = "context";
+  g_map_error[0] = 0;
+  cudaError_t ce = bind_context();
+  if (ce != cudaSuccess) return ce;
   const long long BH = a.B * a.H;
   CUtensorMap mq, mk, mv, mdo, mdq;
+  g_bwd_stage = "tensor map of dO";
   const bool do_ok = a.act_bthd ? make_map_bthd(&mdo, a.d_o, a.B, a.H, a.T, a.D, kBF16, bwd::BM)
                                 : make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM);
-  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM) || !do_ok ||
-      !make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH) || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH) ||
-      !make_map_f32(&mdq, w.dq_acc, BH, a.T))
-    return cudaErrorInvalidValue;
-  cudaError_t e = simt::launch_prep(a, w.rowdot, w.dq_acc, w.counter);
+  if (!do_ok) return cudaErrorInvalidValue;
+  g_bwd_stage = "tensor map of q";
+  if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, bwd::BM)) return cudaErrorInvalidValue;
+  g_bwd_stage = "tensor map of k";
+  if (!make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH)) return cudaErrorInvalidValue;
+  g_bwd_stage = "tensor map of v";
+  if (!make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH)) return cudaErrorInvalidValue;
+  g_bwd_stage = "tensor map of the dQ accumulator";
+  if (!make_map_f32(&mdq, w.dq_acc, BH, a.T)) return cudaErrorInvalidValue;
+  g_bwd_stage = "prep";
+  // deterministic: the dQ accumulator is written by stores (key tile 0 first), not zeroed
+  cudaError_t e = simt::launch_prep(a, w.rowdot, a.deterministic ? nullptr : w.dq_acc, w.counter, w.ready,
+                                    w.n_ready);
   if (e != cudaSuccess) return e;
-  auto kern = a.act_bthd ? bwd::bwd_kernel<kBF16, true> : bwd::bwd_kernel<kBF16, false>;
+  g_bwd_stage = "kernel";
+  auto kern = a.deterministic ? (a.act_bthd ? bwd::bwd_kernel<kBF16, true, true> : bwd::bwd_kernel<kBF16, false, true>)
+                              : (a.act_bthd ? bwd::bwd_kernel<kBF16, true, false> : bwd::bwd_kernel<kBF16, false, false>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nkt = (a.T + bwd::BN - 1) / bwd::BN;
@@ -1816,8 +1904,9 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   const unsigned grid = (unsigned)std::min<long long>(n_items, num_sms());
   e = launch_pdl(kern, dim3(grid), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo, mdq,
                  a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv, a.dlog_gain ? w.gain_part : nullptr,
-                 w.counter, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
+                 w.counter, w.ready, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
   if (e != cudaSuccess) return e;
+  g_bwd_stage = "cast";
   return simt::launch_cast_dq(a, w.dq_acc, w.gain_part, (int)nkt);
 }
 

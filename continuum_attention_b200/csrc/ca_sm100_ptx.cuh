@@ -163,6 +163,57 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// 3-D tiled store of a shared-memory box into global memory (rows outside the
+// tensor are skipped), tracked by the issuing thread's bulk async-groups.  Lane 0.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile(
+      "{\n\t" CA_LANE0_PRED
+      "@l0 cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// order this thread's completed bulk (async-proxy) global writes with its later
+// generic-proxy accesses, and the reverse
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// *p += v with release semantics at GPU scope (no return value)
+__device__ __forceinline__ void red_release_add_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until *p >= target (a counter other CTAs of the same launch raise), with
+// the same 2 s limit, status word and abort flag as mbar_wait.  Whole warp,
+// converged; every lane returns the same answer.
+__device__ __forceinline__ bool wait_count(const unsigned* p, unsigned target, volatile int* abort_flag) {
+  bool done = ld_acquire_gpu(p) >= target;
+  if (__all_sync(0xffffffffu, done)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    done = ld_acquire_gpu(p) >= target;
+    if (__all_sync(0xffffffffu, done)) return true;
+    if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if ((threadIdx.x & 31) == 0) {
+        atomicCAS(&g_device_status, 0, 5);
+        *abort_flag = 1;
+      }
+      __syncwarp();
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   // (the unused operand makes this an operand-carrying asm, so %% is unescaped as elsewhere)
   asm volatile("{\n\t" CA_LANE0_PRED "@l0 cp.async.bulk.commit_group;\n\t}" ::"n"(0) : "memory");

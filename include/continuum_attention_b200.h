@@ -142,6 +142,27 @@ int ca_backward_ex(const void* q, const void* k, const void* v, const void* o, c
                    int64_t B, int64_t H, int64_t T, int64_t D,
                    int dtype, int impl, int layout, void* stream);
 
+/* Flags of ca_backward_ex2. */
+enum ca_backward_flags {
+  /* dQ summed in one fixed order, so every output is bitwise reproducible run to
+   * run (dK, dV and d log_gain always are): each dQ tile takes its key tiles'
+   * contributions in ascending key-tile order.  Needs the tcgen05 kernels
+   * (bf16/f16, D = 64); with the CUDA-core kernels the call returns
+   * CA_ERR_UNSUPPORTED. */
+  CA_BWD_DETERMINISTIC = 1
+};
+
+/* ca_backward_ex with flags (ca_backward_flags).  Replaces the same reference code
+ * as ca_backward; CA_BWD_DETERMINISTIC is the counterpart of the fixed per-tile
+ * accumulation order of the reference backward (gq add_ per query tile,
+ * cuda/continuum_attention.py:754-764). */
+int ca_backward_ex2(const void* q, const void* k, const void* v, const void* o, const float* o_f32,
+                    const void* d_o, const float* log_gain, const float* row_stats,
+                    void* dq, void* dk, void* dv, float* dlog_gain,
+                    void* workspace, size_t workspace_bytes,
+                    int64_t B, int64_t H, int64_t T, int64_t D,
+                    int dtype, int impl, int layout, int flags, void* stream);
+
 /*
  * Backward without caller-provided scratch.  No counterpart in the reference
  * (its backward allocates through torch inside the extension).

@@ -130,3 +130,19 @@ def test_rope_argument_checks_on_cpu():
     st, msg = _status_and_msg(lib.ca_rope_qkv_forward(fake, fake, fake, fake, fake, 1, 4, 2, 12, 1, None))
     assert st == 2 and "multiple of 8" in msg
     assert lib.ca_rope_qkv_forward(None, None, None, None, None, 0, 4, 2, 8, 1, None) == 0
+
+
+def test_backward_flags_checked_on_cpu():
+    lib = _native.lib()
+    fake = ctypes.c_void_p(256)
+    args = (fake, fake, fake, fake, None, fake, fake, fake, fake, fake, fake, None, fake, 1 << 20,
+            1, 2, 256, 64, 1, 0, 0)
+    st, msg = _status_and_msg(lib.ca_backward_ex2(*args, 4, None))
+    assert st == 1 and "flags" in msg
+    # deterministic dQ needs the tcgen05 kernels: the CUDA-core family is refused up front
+    st, msg = _status_and_msg(lib.ca_backward_ex2(*args[:-2], 1, 0, _native.CA_BWD_DETERMINISTIC, None))
+    assert st == 2 and "deterministic" in msg
+    st, msg = _status_and_msg(lib.ca_backward_ex2(fake, fake, fake, fake, None, fake, fake, fake, fake, fake, fake,
+                                                  None, fake, 1 << 20, 1, 2, 256, 32, 1, 0, 0,
+                                                  _native.CA_BWD_DETERMINISTIC, None))
+    assert st == 2 and "deterministic" in msg
