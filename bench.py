@@ -122,6 +122,14 @@ def _gpu_local_cpus(local: int):
         os.sched_setaffinity(0, old)
 
 
+def _is_float(x):
+    try:
+        float(x)
+        return True
+    except ValueError:
+        return False
+
+
 class ClockSampler:
     """Samples nvidia-smi SM clocks and throttle reasons while running."""
 
@@ -173,8 +181,10 @@ class ClockSampler:
             return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        power = [float(p[3]) for p in (l.split(",") for l in self.lines) if len(p) >= 9 and _is_float(p[3])]
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows),
+                "power_w": statistics.median(power) if power else None}
 
 
 def _dist_setup():
@@ -364,19 +374,10 @@ def run_decoder(args, world, rank, local, steps: int, warmup: int):
             "final_loss": float(loss.item()) if loss is not None else None, "data": "synthetic uniform bytes"}
 
 
-def run_config3_sharded(world, rank, local, T: int = 16384, steps: int = 5, warmup: int = 2):
-    """BASELINE config 3 across the ranks: [8,16,T,64] bf16 with q, k ~ N(0, 2^2) (score
-    std about 4) and a seeded 10% of keys duplicating their left neighbour, fwd+bwd
-    through the public op.  The 128 head-sequences are split into contiguous slices,
-    one per rank, with no communication: the total work is fixed, so this is the
-    operator's strong scaling.  Returns a dict for the JSON line."""
-    import continuum_attention_b200 as ca
-    from continuum_attention_b200.distributed import bh_shard
-    B, H, D = 8, 16, 64
-    start, end = bh_shard(B, H, world, rank)
-    n = end - start
-    dev = torch.device("cuda", local)
-    g = torch.Generator(device="cpu").manual_seed(3000 + rank)
+def _config3_inputs(n, T, D, dev, seed):
+    """n head-sequences of BASELINE config 3's input recipe: q, k ~ N(0, 2^2) (score std
+    about 4), a seeded 10% of keys duplicating their left neighbour, bf16."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
     q = (torch.randn(1, n, T, D, generator=g) * 2).to(dev, torch.bfloat16)
     k = torch.randn(1, n, T, D, generator=g) * 2
     dup = torch.rand(T, generator=g) < 0.1
@@ -385,29 +386,80 @@ def run_config3_sharded(world, rank, local, T: int = 16384, steps: int = 5, warm
         k[:, :, j] = k[:, :, j - 1]
     k = k.to(dev, torch.bfloat16)
     v, dy = (torch.randn(1, n, T, D, generator=g).to(dev, torch.bfloat16) for _ in range(2))
-    lg = torch.zeros(n, device=dev, requires_grad=True)   # gain 1; one entry per head-sequence of the slice
+    return q, k, v, dy
 
-    def step():
+
+def _config3_time(q, k, v, dy, steps, warmup, world, local, sample_clocks):
+    """Times fwd+bwd of the public op on one slice; returns (max-over-ranks ms for all
+    steps, forward ms per step, backward ms per step, clock summary or None)."""
+    import continuum_attention_b200 as ca
+    lg = torch.zeros(q.shape[1], device=q.device, requires_grad=True)
+    stream = torch.cuda.current_stream(q.device)
+
+    def step(ev_mid=None):
         qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
         y = ca.continuum_attention(qq, kk, vv, lg, 128)
+        if ev_mid is not None:
+            ev_mid.record(stream)
         return torch.autograd.grad(y, (qq, kk, vv, lg), dy)
 
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps + 1)]
+    clk = ClockSampler(local) if sample_clocks else None
+    if clk is not None:
+        clk.__enter__()
+        time.sleep(0.25)
     _barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
+    evs[0].record(stream)
+    for i in range(steps):
+        step(evs[2 * i + 1])
+        evs[2 * i + 2].record(stream)
     torch.cuda.synchronize()
-    ms = _max_over_ranks(world, e0.elapsed_time(e1))
+    if clk is not None:
+        time.sleep(0.1)
+        clk.__exit__(None, None, None)
+    ms = _max_over_ranks(world, evs[0].elapsed_time(evs[-1]))
+    fwd = statistics.mean(evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(steps))
+    bwd = statistics.mean(evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(steps))
+    return ms, fwd, bwd, (clk.summary() if clk is not None else None)
+
+
+def run_config3_sharded(world, rank, local, T: int = 16384, steps: int = 5, warmup: int = 2):
+    """BASELINE config 3 across the ranks: [8,16,T,64] bf16 with q, k ~ N(0, 2^2) (score
+    std about 4) and a seeded 10% of keys duplicating their left neighbour, fwd+bwd
+    through the public op.  The 128 head-sequences are split into contiguous slices,
+    one per rank, with no communication: the total work is fixed, so this is the
+    operator's strong scaling.  The timed steps carry the SM-clock record of this rank.
+    On one GPU the eighth-size slice that each of 8 ranks runs is timed as well
+    ("slice_of_8"), so that the per-head-sequence cost of the two slice sizes can be
+    compared on the same GPU.  Returns a dict for the JSON line."""
+    from continuum_attention_b200.distributed import bh_shard
+    B, H, D = 8, 16, 64
+    start, end = bh_shard(B, H, world, rank)
+    n = end - start
+    dev = torch.device("cuda", local)
+    q, k, v, dy = _config3_inputs(n, T, D, dev, 3000 + rank)
+    ms, fwd, bwd, clocks = _config3_time(q, k, v, dy, steps, warmup, world, local, sample_clocks=True)
+    del q, k, v, dy
     flops = 4.0 * B * H * T * T * D
-    return {"metric": f"CA fwd+bwd TFLOP/s, BASELINE config 3 at B=8 ([8,16,{T},64] bf16) over all ranks",
-            "value": flops * steps / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": steps,
-            "warmup": warmup, "ms_per_step": ms / steps, "head_sequences_per_rank": n, "scaling": "strong",
-            "parallelism": f"bh-shard x{world}", "data": "synthetic (score std 4, 10% duplicated keys)"}
+    out = {"metric": f"CA fwd+bwd TFLOP/s, BASELINE config 3 at B=8 ([8,16,{T},64] bf16) over all ranks",
+           "value": flops * steps / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": steps,
+           "warmup": warmup, "ms_per_step": ms / steps, "forward_ms": fwd, "backward_ms": bwd,
+           "head_sequences_per_rank": n, "scaling": "strong", "clocks": clocks,
+           "parallelism": f"bh-shard x{world}", "data": "synthetic (score std 4, 10% duplicated keys)"}
+    if world == 1:
+        n8 = (B * H) // 8
+        q, k, v, dy = _config3_inputs(n8, T, D, dev, 3000)
+        ms8, fwd8, bwd8, clocks8 = _config3_time(q, k, v, dy, steps, warmup, 1, local, sample_clocks=True)
+        del q, k, v, dy
+        out["slice_of_8"] = {"head_sequences": n8, "ms_per_step": ms8 / steps, "forward_ms": fwd8,
+                             "backward_ms": bwd8, "clocks": clocks8,
+                             "us_per_head_sequence": 1e3 * ms8 / steps / n8,
+                             "us_per_head_sequence_full": 1e3 * ms / steps / n}
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_tinylm(local, steps: int = 50):

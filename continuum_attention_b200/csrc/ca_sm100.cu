@@ -800,13 +800,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const void* __restrict__ vptr,
            const float* __restrict__ log_gain, void* __restrict__ optr, float* __restrict__ o32,
-           float* __restrict__ stats, int BH, int H, int Tn, float inv_sqrt_d, int o_bthd) {
+           float* __restrict__ stats, int BH, int H, int Tn, float inv_sqrt_d, int o_bthd, int grp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqt = (Tn + BM - 1) / BM;
-  const int bh = blockIdx.x % BH;
-  const int qt = nqt - 1 - blockIdx.x / BH;   // heaviest query tiles first
+  // head-sequences in groups of grp, one group after another; inside a group the
+  // heaviest query tiles first (see head_group())
+  const int gi = blockIdx.x / (grp * nqt);
+  const int gr = blockIdx.x - gi * grp * nqt;
+  const int gs = min(grp, BH - gi * grp);
+  const int bh = gi * grp + gr % gs;
+  const int qt = nqt - 1 - gr / gs;
   const int q0 = qt * BM;
   const int nh = 2 * (qt + 1);                // key half-tiles 0 .. 2qt+1 (keys 0 .. q0+127)
 
@@ -970,8 +975,10 @@ __device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tme
   }
 }
 
-// Work item w (heaviest first): key tile kt = w / BH of head-sequence bh = w % BH,
-// with n = nkt - kt query tiles.  Tile t of an item is query tile kt + n - 1 - t:
+// Work item w: head-sequences go in groups of grp (see head_group()), one group
+// after another; inside a group the heaviest items first: key tile kt = r / gs of
+// head-sequence bh = g * grp + r % gs (group g, r = w - g * grp * nkt, gs the
+// group's size), with n = nkt - kt query tiles.  Tile t of an item is query tile kt + n - 1 - t:
 // the last query tile first and the diagonal tile last, so that every item reaches
 // a given query tile at the same offset from its start, and the items of a head,
 // started in key-tile order (heaviest first), reach it in key-tile order too.
@@ -979,10 +986,13 @@ struct Item {
   int bh, kt, j0, n;
   __device__ __forceinline__ int row0(int t) const { return j0 + (n - 1 - t) * BM; }
 };
-__device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
+__device__ __forceinline__ Item decode_item(int w, int BH, int nkt, int grp) {
   Item it;
-  it.bh = w % BH;
-  it.kt = w / BH;
+  const int g = w / (grp * nkt);
+  const int r = w - g * grp * nkt;
+  const int gs = min(grp, BH - g * grp);
+  it.bh = g * grp + r % gs;
+  it.kt = r / gs;
   it.j0 = it.kt * BN;
   it.n = nkt - it.kt;
   return it;
@@ -1005,7 +1015,7 @@ __device__ __forceinline__ Item decode_item(int w, int BH, int nkt) {
 // no zeroing).  Otherwise the contributions are reduce-adds in arrival order.
 template <bool kBF16, bool kDOB, bool kDet>
 __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
-                         const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int n_items,
+                         const CUtensorMap* tdo, const CUtensorMap* tdq, int BH, int nkt, int grp, int n_items,
                          unsigned* counter, unsigned* ready, uint32_t tmem, int H) {
   volatile int* ab = &sm.abort_flag;
   const int lane = threadIdx.x & 31;
@@ -1130,26 +1140,26 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
   };
   bool good = item < n_items;
   if (good) {
-    const Item it = decode_item(item, BH, nkt);
+    const Item it = decode_item(item, BH, nkt, grp);
     load_kv(it);
   }
   publish(good ? item : n_items);
   bool pending = false;   // the previous item's last dQ tile still has to be reduced
-  Item prev = decode_item(0, BH, nkt);
+  Item prev = decode_item(0, BH, nkt, grp);
   while (good) {
-    const Item it = decode_item(item, BH, nkt);
+    const Item it = decode_item(item, BH, nkt, grp);
     // The next item is claimed as late as its first Q/dO prefetch allows (the
     // item's second-to-last tile, or its start when it has one tile), so that the
     // counter hands the heaviest remaining items to the CTAs that free up first.
     // Its K'/V' boxes are prefetched into L2 at once; the shared-memory copy
     // follows when this item's last gradient MMAs have read K'.
     bool has_next = false;
-    Item nx = decode_item(0, BH, nkt);
+    Item nx = decode_item(0, BH, nkt, grp);
     auto claim = [&]() {
       next = fetch();
       has_next = next < n_items;
       if (has_next) {
-        nx = decode_item(next, BH, nkt);
+        nx = decode_item(next, BH, nkt, grp);
         tma_prefetch_l2_3d(tk, 0, max(nx.j0 - KOFF, 0), nx.bh);
         tma_prefetch_l2_3d(tv, 0, max(nx.j0 - KOFF, 0), nx.bh);
       }
@@ -1616,7 +1626,7 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
 // barriers.
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
-                           void* dkp, void* dvp, float* gain_part, int BH, int H, int Tn, int nkt, int n_items,
+                           void* dkp, void* dvp, float* gain_part, int BH, int H, int Tn, int nkt, int grp, int n_items,
                            uint32_t tmem, float inv_sqrt_d) {
   volatile int* ab = &sm.abort_flag;
   uint32_t g0 = 0;
@@ -1632,7 +1642,7 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     named_bar_sync(2, NUM_MATH_WARPS * 32);
     const int item = sm.decision;
     if (item >= n_items) break;
-    const Item it = decode_item(item, BH, nkt);
+    const Item it = decode_item(item, BH, nkt, grp);
     math_item<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, it.bh, it.bh % H, Tn, it.j0, it.kt, nkt,
                      it.n, g0, tmem, inv_sqrt_d, ok);
     ok = ok && !*ab;
@@ -1648,7 +1658,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            const float* __restrict__ stats, const float* __restrict__ rowdot,
            void* __restrict__ dkp, void* __restrict__ dvp,
            float* __restrict__ gain_part, unsigned* __restrict__ counter, unsigned* __restrict__ ready, int BH,
-           int H, int Tn, float inv_sqrt_d) {
+           int H, int Tn, float inv_sqrt_d, int grp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1688,11 +1698,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   pdl_launch_dependents();
 
   if (warp == NUM_MATH_WARPS) {
-    producer<kBF16, kDOB, kDet>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, n_items, counter, ready, tmem,
+    producer<kBF16, kDOB, kDet>(sm, &tm_q, &tm_k, &tm_v, &tm_do, &tm_dq, BH, nkt, grp, n_items, counter, ready, tmem,
                                 H);   // converged
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, n_items, tmem,
+    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, grp, n_items, tmem,
                       inv_sqrt_d);
   }
   tc_fence_before();
@@ -1836,6 +1846,28 @@ bool backward_supported(const BwdArgs& a) {
 int forward_launches(const FwdArgs&) { return 1; }
 int backward_launches(const BwdArgs&) { return 3; }   // prep, kernel, dQ cast (+ d log_gain)
 
+// Work order over head-sequences.  Both kernels hand out their work heaviest first
+// (longest query rows in the forward, key tiles with the most query tiles in the
+// backward), so the CTAs running at one moment work on the same few key / query
+// tile positions of every head-sequence.  At long T with many head-sequences the
+// tiles they read then come from HBM once each: a [8,16,16384,64] backward runs
+// at 1.15x the cost per head-sequence of a 16-head-sequence one, whose concurrent
+// CTAs share each head-sequence's Q/dO tiles in L2 (forward: 1.05x, K/V tiles).
+// So at T >= 4096 the head-sequences go in groups of 16, one group after another,
+// each group heaviest first; shorter sequences keep one group (their whole
+// working set stays in L2, and smaller groups would lengthen the tail of the
+// heaviest-first order).  CA_B200_HEAD_GROUP=<n> overrides the group size
+// (a tuning switch; read once).
+static int head_group(long long BH, long long ntiles) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("CA_B200_HEAD_GROUP");
+    env = e ? std::max(0, atoi(e)) : 0;
+  }
+  long long g = env > 0 ? env : (ntiles >= 32 ? 16 : BH);
+  return (int)std::max<long long>(1, std::min<long long>(g, BH));
+}
+
 // The permuted-key kernels need T a multiple of 16 (whole 16-key chunks in the 5-D view).
 static bool perm_layout(long long T) { return T % 16 == 0 && !perm_disabled(); }
 
@@ -1855,7 +1887,7 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   const long long nqt = (a.T + fwd::BM - 1) / fwd::BM;
   return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(fwd::NUM_THREADS), fwd::kSmemBytes, a.stream, mq, mk, mv,
                     a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d,
-                    a.o_bthd);
+                    a.o_bthd, head_group(BH, nqt));
 }
 
 cudaError_t forward(const FwdArgs& a) { return a.dtype == 1 ? launch_fwd<true>(a) : launch_fwd<false>(a); }
@@ -1904,7 +1936,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   const unsigned grid = (unsigned)std::min<long long>(n_items, num_sms());
   e = launch_pdl(kern, dim3(grid), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo, mdq,
                  a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv, a.dlog_gain ? w.gain_part : nullptr,
-                 w.counter, w.ready, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d);
+                 w.counter, w.ready, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d, head_group(BH, nkt));
   if (e != cudaSuccess) return e;
   g_bwd_stage = "cast";
   return simt::launch_cast_dq(a, w.dq_acc, w.gain_part, (int)nkt);

@@ -135,6 +135,29 @@ def test_reference_cuda_timing_config2():
     assert res["ours fp16"]["total_ms"] < res["reference prefix_v6 fp16"]["total_ms"]
 
 
+def _inputs(shape, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, dy = (torch.randn(shape, generator=g).to("cuda", dtype) for _ in range(4))
+    lg = torch.zeros(shape[1], device="cuda")
+    return tuple(t.requires_grad_(True) for t in (q, k, v, lg)) + (dy,)
+
+
+@pytest.mark.parametrize("shape,dtype", [((2, 16, 2048, 64), torch.float32),
+                                         ((2, 16, 2048, 128), torch.bfloat16),
+                                         ((2, 16, 2048, 128), torch.float32)])
+def test_reference_cuda_timing_other_dtypes_and_widths(shape, dtype):
+    """fp32 at config 2 and head width 128 against the reference's ``prefix`` mode
+    (cuda/continuum_attention.py:670-694, the only mode that takes these inputs), timed
+    like its speed phase; prints one ``REFERENCE_CUDA_B200_OTHER`` JSON line."""
+    sets = [_inputs(shape, dtype, 1700 + s) for s in range(2)]
+    res = {"shape": list(shape), "dtype": str(dtype).replace("torch.", "")}
+    res["reference prefix"] = _timed(_ref("prefix"), sets)
+    res["ours"] = _timed(_ours, sets)
+    res["speedup"] = res["reference prefix"]["total_ms"] / res["ours"]["total_ms"]
+    print("REFERENCE_CUDA_B200_OTHER", json.dumps(res), flush=True)
+    assert res["ours"]["total_ms"] > 0 and res["reference prefix"]["total_ms"] > 0
+
+
 def _cos(a, b):
     a, b = a.detach().double().flatten(), b.detach().double().flatten()
     return float(a @ b / (a.norm() * b.norm()).clamp_min(1e-300))
