@@ -76,26 +76,25 @@ struct __align__(1024) Smem {
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack
 
 // S = Q K_h^T for one half-tile: M = 128 queries, N = 64 keys, K = 64 (4 MMAs)
+// (descriptors: the base one plus byte offset >> 4 in the start-address field, which
+// never carries since shared addresses stay below 256 KB)
 __device__ __forceinline__ void issue_s(uint32_t q_saddr, uint32_t k_saddr, uint32_t d_tmem, uint32_t idesc) {
+  const uint64_t a = sdesc_sw128(q_saddr, 16, 1024), b = sdesc_sw128(k_saddr, 16, 1024);
 #pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    const uint64_t a = sdesc_sw128(q_saddr + kk * 32, 16, 1024);
-    const uint64_t b = sdesc_sw128(k_saddr + kk * 32, 16, 1024);
-    mma_ss(d_tmem, a, b, idesc, kk > 0 ? 1u : 0u);
-  }
+  for (int kk = 0; kk < HD / 16; ++kk) mma_ss(d_tmem, a + 2 * kk, b + 2 * kk, idesc, kk > 0 ? 1u : 0u);
 }
 
 // O += P V'_h over the half-tile's 64 keys: hi and lo parts of P, 16 keys per MMA,
 // A from TMEM (16 columns per 16 keys: 8 of hi pairs, then 8 of lo pairs)
 __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_saddr, uint32_t idesc,
                                          bool accumulate) {
+  const uint64_t b = sdesc_sw128(v_saddr, 16384, 1024);   // V': MN-major, 2048 bytes per 16 keys
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
 #pragma unroll
     for (int kk = 0; kk < HB / 16; ++kk) {
-      const uint64_t b = sdesc_sw128(v_saddr + kk * 2048, 16384, 1024);   // V': MN-major
       const uint32_t acc = (accumulate || part > 0 || kk > 0) ? 1u : 0u;
-      mma_ts(o_tmem, p_tmem + 16 * kk + 8 * part, b, idesc, acc);
+      mma_ts(o_tmem, p_tmem + 16 * kk + 8 * part, b + 128 * kk, idesc, acc);
     }
   }
 }
@@ -934,43 +933,43 @@ struct __align__(1024) Smem {
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
+// The shared-memory descriptors of one operand differ only in the start-address
+// field ([0,14), address >> 4), which never carries (shared addresses stay below
+// 256 KB): each is its base descriptor plus the byte offset >> 4, one add per MMA.
 template <bool kBF16>
 __device__ __forceinline__ void issue_s_dp(const Smem& sm, int st, uint32_t tmem, uint32_t idesc) {
-  const uint32_t qa = smem_u32(sm.q[st]), oa = smem_u32(sm.dout[st]);
-  const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
+  const uint64_t dq = sdesc_sw128(smem_u32(sm.q[st]), 16, 1024), dk = sdesc_sw128(smem_u32(sm.k), 16, 1024);
+  const uint64_t ddo = sdesc_sw128(smem_u32(sm.dout[st]), 16, 1024), dv = sdesc_sw128(smem_u32(sm.v), 16, 1024);
 #pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    mma_ss(tmem + T_S, sdesc_sw128(qa + kk * 32, 16, 1024), sdesc_sw128(ka + kk * 32, 16, 1024), idesc,
-           kk > 0 ? 1u : 0u);
-  }
+  for (int kk = 0; kk < HD / 16; ++kk)   // 32 bytes of K per step
+    mma_ss(tmem + T_S, dq + 2 * kk, dk + 2 * kk, idesc, kk > 0 ? 1u : 0u);
 #pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    mma_ss(tmem + T_DP, sdesc_sw128(oa + kk * 32, 16, 1024), sdesc_sw128(va + kk * 32, 16, 1024), idesc,
-           kk > 0 ? 1u : 0u);
-  }
+  for (int kk = 0; kk < HD / 16; ++kk)
+    mma_ss(tmem + T_DP, ddo + 2 * kk, dv + 2 * kk, idesc, kk > 0 ? 1u : 0u);
 }
 
 template <bool kBF16>
 __device__ __forceinline__ void issue_grads(const Smem& sm, int st, uint32_t tmem, bool first, uint32_t id_mn,
                                             uint32_t id_dq) {
-  const uint32_t pa = smem_u32(sm.p[0]), da = smem_u32(sm.ds[0]);
-  const uint32_t qa = smem_u32(sm.q[st]), oa = smem_u32(sm.dout[st]);
-  const uint32_t ka = smem_u32(sm.k) + KOFF * 128;
+  const uint64_t dp = sdesc_sw128(smem_u32(sm.p[0]), HALF_BYTES, 1024);
+  const uint64_t dds = sdesc_sw128(smem_u32(sm.ds[0]), HALF_BYTES, 1024);
+  const uint64_t dq = sdesc_sw128(smem_u32(sm.q[st]), 16384, 1024);
+  const uint64_t ddo = sdesc_sw128(smem_u32(sm.dout[st]), 16384, 1024);
+  const uint64_t dsk = sdesc_sw128(smem_u32(sm.ds[0]), 16, 1024);
+  const uint64_t dk = sdesc_sw128(smem_u32(sm.k) + KOFF * 128, 16384, 1024);
 #pragma unroll
-  for (int kk = 0; kk < BM / 16; ++kk) {   // K = query rows, 16 per step
+  for (int kk = 0; kk < BM / 16; ++kk) {   // K = query rows, 16 per step (2048 bytes)
     const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
     // dV += P^T dO : A = P (MN-major, M = keys), B = dO (MN-major, N = d)
-    mma_ss(tmem + T_DV, sdesc_sw128(pa + kk * 2048, HALF_BYTES, 1024), sdesc_sw128(oa + kk * 2048, 16384, 1024),
-           id_mn, acc);
+    mma_ss(tmem + T_DV, dp + 128 * kk, ddo + 128 * kk, id_mn, acc);
     // dK += dS^T Q
-    mma_ss(tmem + T_DK, sdesc_sw128(da + kk * 2048, HALF_BYTES, 1024), sdesc_sw128(qa + kk * 2048, 16384, 1024),
-           id_mn, acc);
+    mma_ss(tmem + T_DK, dds + 128 * kk, dq + 128 * kk, id_mn, acc);
   }
 #pragma unroll
   for (int kk = 0; kk < BN / 16; ++kk) {   // K = keys, 16 per step
-    // dQ = dS K : A = dS (K-major, M = queries), B = K rows j0.. (MN-major, N = d)
-    const uint32_t a_addr = da + (kk / 4) * HALF_BYTES + (kk % 4) * 32;
-    mma_ss(tmem + T_DQ, sdesc_sw128(a_addr, 16, 1024), sdesc_sw128(ka + kk * 2048, 16384, 1024), id_dq,
+    // dQ = dS K : A = dS (K-major, M = queries; key half kk / 4, 32 bytes per step),
+    // B = K rows j0.. (MN-major, N = d, 2048 bytes per step)
+    mma_ss(tmem + T_DQ, dsk + (HALF_BYTES >> 4) * (kk / 4) + 2 * (kk % 4), dk + 128 * kk, id_dq,
            kk > 0 ? 1u : 0u);
   }
 }
