@@ -1411,7 +1411,7 @@ __device__ __forceinline__ void stage_dq(Smem& sm, int r, int qk, const uint32_t
 // query tiles being global tiles g0 .. g0+n_tiles-1 of this CTA.
 template <bool kBF16>
 __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
-                          void* dkp, void* dvp, float* gain_part, int bh, int h, int Tn, int j0,
+                          const CUtensorMap* tm_dk, const CUtensorMap* tm_dv, float* gain_part, int bh, int h, int Tn, int j0,
                           int kt, int nkt, int n_tiles, uint32_t g0, uint32_t tmem, float inv_sqrt_d, bool& ok) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1591,27 +1591,37 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
     tmem_ld32(tmem + lane_base + (is_k ? T_DK : T_DV) + c0, av);
     tmem_ld_wait();
     tmem_reg_fence(av);
-    const int key = j0 + r;
-    if (ok && key < Tn) {
-      uint16_t* base = reinterpret_cast<uint16_t*>(is_k ? dkp : dvp) + ((size_t)bh * Tn + key) * HD + c0;
-      uint4* dst = reinterpret_cast<uint4*>(base);
+    // staged in the P buffer (free once the item's last gradient MMAs have completed)
+    // as the TMA store box: dV in p[0], dK in p[1], row r = key j0 + r, 128-byte rows
+    // with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)), so
+    // that the 32 rows of a warp hit distinct banks
+    uint8_t* const srow = sm.p[is_k ? 1 : 0] + (uint32_t)r * 128;
 #pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        uint32_t w[4];
+    for (int x = 0; x < 4; ++x) {
+      uint32_t w[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float a0 = __uint_as_float(av[8 * x + 2 * u]), a1 = __uint_as_float(av[8 * x + 2 * u + 1]);
-          w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
-        }
-        dst[x] = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int u = 0; u < 4; ++u) {
+        const float a0 = __uint_as_float(av[8 * x + 2 * u]), a1 = __uint_as_float(av[8 * x + 2 * u + 1]);
+        w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
       }
+      const int chunk = 4 * (qk & 1) + x;
+      *reinterpret_cast<uint4*>(srow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+    fence_proxy_async_smem();
   }
   // d log_gain partial of this key tile: sum over the CTA of dS * s (gsum holds scale * that)
   gsum = (gsum + (gsum2.x + gsum2.y)) / scale;
   for (int off = 16; off > 0; off >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, off);
   if (lane == 0) sm.red[warp] = gsum;
   named_bar_sync(1, NUM_MATH_WARPS * 32);
+  // dK, dV out with two TMA stores (whole 128-byte rows; rows past T are not
+  // written); the P buffer is reused only after they have read it (math_warps waits
+  // for that at the item boundary)
+  if (threadIdx.x == 0 && ok) {
+    tma_store_3d(tm_dv, sm.p[0], 0, j0, bh);
+    tma_store_3d(tm_dk, sm.p[1], 0, j0, bh);
+    bulk_commit_group();
+  }
   if (gain_part && threadIdx.x == 0) {
     float tsum = 0.f;
     for (int w = 0; w < NUM_MATH_WARPS; ++w) tsum += sm.red[w];
@@ -1625,8 +1635,8 @@ __device__ void math_item(Smem& sm, const float* log_gain, const float* stats, c
 // barriers.
 template <bool kBF16>
 __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, const float* rowdot,
-                           void* dkp, void* dvp, float* gain_part, int BH, int H, int Tn, int nkt, int grp, int n_items,
-                           uint32_t tmem, float inv_sqrt_d) {
+                           const CUtensorMap* tm_dk, const CUtensorMap* tm_dv, float* gain_part, int BH, int H, int Tn,
+                           int nkt, int grp, int n_items, uint32_t tmem, float inv_sqrt_d) {
   volatile int* ab = &sm.abort_flag;
   uint32_t g0 = 0;
   uint32_t published = 0;
@@ -1634,6 +1644,9 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
   while (true) {
     named_bar_sync(2, NUM_MATH_WARPS * 32);
     if (threadIdx.x == 0) {
+      // the previous item's dK/dV stores have read the P buffer, which the next
+      // item's first P/dS overwrites (no bulk group: returns at once)
+      bulk_wait_group_read0();
       const bool got = ok && mbar_wait(&sm.bar_item, published & 1, ab);
       sm.decision = got ? sm.item : n_items;
     }
@@ -1642,20 +1655,21 @@ __device__ void math_warps(Smem& sm, const float* log_gain, const float* stats, 
     const int item = sm.decision;
     if (item >= n_items) break;
     const Item it = decode_item(item, BH, nkt, grp);
-    math_item<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, it.bh, it.bh % H, Tn, it.j0, it.kt, nkt,
-                     it.n, g0, tmem, inv_sqrt_d, ok);
+    math_item<kBF16>(sm, log_gain, stats, rowdot, tm_dk, tm_dv, gain_part, it.bh, it.bh % H, Tn, it.j0, it.kt,
+                     nkt, it.n, g0, tmem, inv_sqrt_d, ok);
     ok = ok && !*ab;
     g0 += it.n;
   }
+  if (threadIdx.x == 0) bulk_wait_group0();   // the last dK/dV stores have landed
 }
 
 template <bool kBF16, bool kDOB, bool kDet>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-           const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ log_gain,
+           const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+           const __grid_constant__ CUtensorMap tm_dv, const float* __restrict__ log_gain,
            const float* __restrict__ stats, const float* __restrict__ rowdot,
-           void* __restrict__ dkp, void* __restrict__ dvp,
            float* __restrict__ gain_part, unsigned* __restrict__ counter, unsigned* __restrict__ ready, int BH,
            int H, int Tn, float inv_sqrt_d, int grp) {
   extern __shared__ uint8_t smem_raw[];
@@ -1682,6 +1696,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
       tma_prefetch_desc(&tm_dq);
+      tma_prefetch_desc(&tm_dk);
+      tma_prefetch_desc(&tm_dv);
     }
     __syncwarp();
     tmem_alloc(&sm.tmem_base, TMEM_COLS);
@@ -1701,7 +1717,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                                 H);   // converged
     __syncwarp();
   } else {
-    math_warps<kBF16>(sm, log_gain, stats, rowdot, dkp, dvp, gain_part, BH, H, Tn, nkt, grp, n_items, tmem,
+    math_warps<kBF16>(sm, log_gain, stats, rowdot, &tm_dk, &tm_dv, gain_part, BH, H, Tn, nkt, grp, n_items, tmem,
                       inv_sqrt_d);
   }
   tc_fence_before();
@@ -1905,7 +1921,7 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   cudaError_t ce = bind_context();
   if (ce != cudaSuccess) return ce;
   const long long BH = a.B * a.H;
-  CUtensorMap mq, mk, mv, mdo, mdq;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
   g_bwd_stage = "tensor map of dO";
   const bool do_ok = a.act_bthd ? make_map_bthd(&mdo, a.d_o, a.B, a.H, a.T, a.D, kBF16, bwd::BM)
                                 : make_map(&mdo, a.d_o, BH, a.T, a.D, kBF16, bwd::BM);
@@ -1916,6 +1932,9 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   if (!make_map(&mk, a.k, BH, a.T, a.D, kBF16, bwd::KH)) return cudaErrorInvalidValue;
   g_bwd_stage = "tensor map of v";
   if (!make_map(&mv, a.v, BH, a.T, a.D, kBF16, bwd::KH)) return cudaErrorInvalidValue;
+  g_bwd_stage = "tensor maps of dk, dv";
+  if (!make_map(&mdk, a.dk, BH, a.T, a.D, kBF16, bwd::BN) || !make_map(&mdv, a.dv, BH, a.T, a.D, kBF16, bwd::BN))
+    return cudaErrorInvalidValue;
   g_bwd_stage = "tensor map of the dQ accumulator";
   if (!make_map_f32(&mdq, w.dq_acc, BH, a.T)) return cudaErrorInvalidValue;
   g_bwd_stage = "prep";
@@ -1933,8 +1952,8 @@ static cudaError_t launch_bwd(const BwdArgs& a, const BwdWorkspace& w) {
   // persistent: one CTA per SM (at most one per work item); items beyond the first
   // gridDim.x come from the counter, which the prep kernel has zeroed
   const unsigned grid = (unsigned)std::min<long long>(n_items, num_sms());
-  e = launch_pdl(kern, dim3(grid), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo, mdq,
-                 a.log_gain, a.row_stats, (const float*)w.rowdot, a.dk, a.dv, a.dlog_gain ? w.gain_part : nullptr,
+  e = launch_pdl(kern, dim3(grid), dim3(bwd::NUM_THREADS), bwd::kSmemBytes, a.stream, mq, mk, mv, mdo, mdq, mdk,
+                 mdv, a.log_gain, a.row_stats, (const float*)w.rowdot, a.dlog_gain ? w.gain_part : nullptr,
                  w.counter, w.ready, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d, head_group(BH, nkt));
   if (e != cudaSuccess) return e;
   g_bwd_stage = "cast";
