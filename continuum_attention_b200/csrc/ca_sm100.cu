@@ -463,9 +463,58 @@ __device__ __forceinline__ float perm_max64(const uint32_t (&a)[32], const uint3
   return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
+// The epilogue's output rows leave through shared memory and TMA stores: each math
+// thread writes its row of O (dtype) and of the fp32 O into the K/V' ring (free once
+// the last P V' has completed), 128-byte rows with the 128-byte swizzle (16-byte chunk
+// c of row r at chunk c ^ (r & 7), so the 32 rows of a warp hit distinct banks); after
+// the math warps sync, thread 0 stores the tiles with whole-row writes (rows past T are
+// not written) and waits for them.  O goes to v[0..1] (128 rows x 128 bytes), the fp32
+// O to k[0..3] as two 32-column halves.  Scattered per-thread 16-byte stores of the same
+// rows cost one L1 tag lookup per row per instruction.
 template <bool kBF16>
-__device__ void math_warps_perm(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32,
-                                float* stats, int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d,
+__device__ __forceinline__ void store_out_rows(Smem& sm, const float (&acc)[HD], float inv, int r, bool has32,
+                                               const CUtensorMap* tm_o, const CUtensorMap* tm_o32, int bh, int H,
+                                               int q0, int o_bthd) {
+  uint8_t* const orow = &sm.v[0][0] + (uint32_t)r * 128;
+#pragma unroll
+  for (int c = 0; c < HD / 8; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a0 = acc[8 * c + 2 * u] * inv, a1 = acc[8 * c + 2 * u + 1] * inv;
+      w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+    }
+    *reinterpret_cast<uint4*>(orow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (has32) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      uint8_t* const row32 = &sm.k[0][0] + hf * (BM * 128) + (uint32_t)r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int d = 32 * hf + 4 * c;
+        *reinterpret_cast<float4*>(row32 + ((c ^ (r & 7)) << 4)) =
+            make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  named_bar_sync(1, BM);
+  if (threadIdx.x == 0 && !sm.abort_flag) {
+    if (o_bthd) tma_store_4d(tm_o, &sm.v[0][0], 0, bh % H, q0, bh / H);
+    else tma_store_3d(tm_o, &sm.v[0][0], 0, q0, bh);
+    if (has32) {
+      tma_store_3d(tm_o32, &sm.k[0][0], 0, q0, bh);
+      tma_store_3d(tm_o32, &sm.k[0][0] + BM * 128, 32, q0, bh);
+    }
+    bulk_commit_group();
+    bulk_wait_group0();
+  }
+}
+
+template <bool kBF16>
+__device__ void math_warps_perm(Smem& sm, const void* vptr, const float* log_gain, const CUtensorMap* tm_o,
+                                const CUtensorMap* tm_o32, float* o32, float* stats, int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d,
                                 int H, int o_bthd) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -590,50 +639,46 @@ __device__ void math_warps_perm(Smem& sm, const void* vptr, const float* log_gai
   tmem_ld_wait();
   tmem_reg_fence(oa[0]);
   tmem_reg_fence(oa[1]);
-  if (!ok || !row_ok) return;
   float acc[HD];
 #pragma unroll
   for (int d = 0; d < HD; ++d) acc[d] = __uint_as_float(oa[d / 32][d % 32]);
   const size_t row = (size_t)bh * Tn + i;
-  if (bpend != 0.f) {
-    const uint16_t* vr = reinterpret_cast<const uint16_t*>(vptr) + row * HD;
+  if (ok && row_ok && bpend != 0.f) {
+    // v of key i, eight 16-byte loads
+    const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(vptr) + row * HD);
+    uint4 vq[HD / 8];
 #pragma unroll
-    for (int d = 0; d < HD; ++d) {
-      const uint32_t bits = (uint32_t)vr[d];
-      float vv;
-      if (kBF16) vv = __uint_as_float(bits << 16);
-      else vv = __half2float(__ushort_as_half((unsigned short)bits));
-      acc[d] = fmaf(bpend, vv, acc[d]);
+    for (int c = 0; c < HD / 8; ++c) vq[c] = __ldg(vr + c);
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+      const uint32_t wv[4] = {vq[c].x, vq[c].y, vq[c].z, vq[c].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float v0, v1;
+        if (kBF16) {
+          v0 = __uint_as_float(wv[u] << 16);
+          v1 = __uint_as_float(wv[u] & 0xffff0000u);
+        } else {
+          v0 = __half2float(__ushort_as_half((unsigned short)(wv[u] & 0xffffu)));
+          v1 = __half2float(__ushort_as_half((unsigned short)(wv[u] >> 16)));
+        }
+        acc[8 * c + 2 * u] = fmaf(bpend, v0, acc[8 * c + 2 * u]);
+        acc[8 * c + 2 * u + 1] = fmaf(bpend, v1, acc[8 * c + 2 * u + 1]);
+      }
     }
   }
   const float z = z2.x + z2.y;
   const float inv = 1.f / z;
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + act_row(row, Tn, H, o_bthd) * HD);
-#pragma unroll
-  for (int c = 0; c < HD / 8; ++c) {
-    uint32_t w[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float a0 = acc[8 * c + 2 * u] * inv, a1 = acc[8 * c + 2 * u + 1] * inv;
-      w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
-    }
-    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-  if (o32) {
-    float4* d32 = reinterpret_cast<float4*>(o32 + row * HD);
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c)
-      d32[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
-  }
-  if (stats) {
+  store_out_rows<kBF16>(sm, acc, inv, r, o32 != nullptr, tm_o, tm_o32, bh, H, q0, o_bthd);
+  if (stats && ok && row_ok) {
     stats[2 * row] = m_used;
     stats[2 * row + 1] = z;
   }
 }
 
 template <bool kBF16>
-__device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, void* optr, float* o32, float* stats,
-                           int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d, int H,
+__device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, const CUtensorMap* tm_o,
+                           const CUtensorMap* tm_o32, float* o32, float* stats, int bh, int h, int Tn, int q0, int nh, uint32_t tmem, float inv_sqrt_d, int H,
                            int o_bthd) {
   volatile int* ab = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -753,42 +798,38 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
   tmem_ld_wait();
   tmem_reg_fence(oa[0]);
   tmem_reg_fence(oa[1]);
-  if (!ok || !row_ok) return;
   float acc[HD];
 #pragma unroll
   for (int d = 0; d < HD; ++d) acc[d] = __uint_as_float(oa[d / 32][d % 32]);
   const size_t row = (size_t)bh * Tn + i;
-  if (bpend != 0.f) {
-    const uint16_t* vr = reinterpret_cast<const uint16_t*>(vptr) + row * HD;
+  if (ok && row_ok && bpend != 0.f) {
+    // v of key i, eight 16-byte loads
+    const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(vptr) + row * HD);
+    uint4 vq[HD / 8];
 #pragma unroll
-    for (int d = 0; d < HD; ++d) {
-      const uint32_t bits = (uint32_t)vr[d];
-      float vv;
-      if (kBF16) vv = __uint_as_float(bits << 16);
-      else vv = __half2float(__ushort_as_half((unsigned short)bits));
-      acc[d] = fmaf(bpend, vv, acc[d]);
+    for (int c = 0; c < HD / 8; ++c) vq[c] = __ldg(vr + c);
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+      const uint32_t wv[4] = {vq[c].x, vq[c].y, vq[c].z, vq[c].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float v0, v1;
+        if (kBF16) {
+          v0 = __uint_as_float(wv[u] << 16);
+          v1 = __uint_as_float(wv[u] & 0xffff0000u);
+        } else {
+          v0 = __half2float(__ushort_as_half((unsigned short)(wv[u] & 0xffffu)));
+          v1 = __half2float(__ushort_as_half((unsigned short)(wv[u] >> 16)));
+        }
+        acc[8 * c + 2 * u] = fmaf(bpend, v0, acc[8 * c + 2 * u]);
+        acc[8 * c + 2 * u + 1] = fmaf(bpend, v1, acc[8 * c + 2 * u + 1]);
+      }
     }
   }
   z += z2.x + z2.y;
   const float inv = 1.f / z;
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(optr) + act_row(row, Tn, H, o_bthd) * HD);
-#pragma unroll
-  for (int c = 0; c < HD / 8; ++c) {
-    uint32_t w[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float a0 = acc[8 * c + 2 * u] * inv, a1 = acc[8 * c + 2 * u + 1] * inv;
-      w[u] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
-    }
-    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-  if (o32) {
-    float4* d32 = reinterpret_cast<float4*>(o32 + row * HD);
-#pragma unroll
-    for (int c = 0; c < HD / 4; ++c)
-      d32[c] = make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
-  }
-  if (stats) {   // nullptr: inference, no backward follows
+  store_out_rows<kBF16>(sm, acc, inv, r, o32 != nullptr, tm_o, tm_o32, bh, H, q0, o_bthd);
+  if (stats && ok && row_ok) {   // nullptr: inference, no backward follows
     stats[2 * row] = m_used;
     stats[2 * row + 1] = z;
   }
@@ -797,8 +838,9 @@ __device__ void math_warps(Smem& sm, const void* vptr, const float* log_gain, vo
 template <bool kBF16, bool kPerm>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
 fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-           const __grid_constant__ CUtensorMap tm_v, const void* __restrict__ vptr,
-           const float* __restrict__ log_gain, void* __restrict__ optr, float* __restrict__ o32,
+           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+           const __grid_constant__ CUtensorMap tm_o32, const void* __restrict__ vptr,
+           const float* __restrict__ log_gain, float* __restrict__ o32,
            float* __restrict__ stats, int BH, int H, int Tn, float inv_sqrt_d, int o_bthd, int grp) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -834,6 +876,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      if (o32) tma_prefetch_desc(&tm_o32);
     }
     __syncwarp();
     tmem_alloc(&sm.tmem_base, TMEM_COLS);
@@ -852,10 +896,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     producer<kBF16, kPerm>(sm, &tm_q, &tm_k, &tm_v, bh, q0, nh, tmem);   // whole warp, converged
     __syncwarp();
   } else if (kPerm) {
-    math_warps_perm<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H,
+    math_warps_perm<kBF16>(sm, vptr, log_gain, &tm_o, &tm_o32, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H,
                            o_bthd);
   } else {
-    math_warps<kBF16>(sm, vptr, log_gain, optr, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H, o_bthd);
+    math_warps<kBF16>(sm, vptr, log_gain, &tm_o, &tm_o32, o32, stats, bh, bh % H, Tn, q0, nh, tmem, inv_sqrt_d, H,
+                      o_bthd);
   }
   tc_fence_before();
   __syncthreads();
@@ -1896,12 +1941,22 @@ static cudaError_t launch_fwd(const FwdArgs& a) {
   const bool k_ok = perm ? make_map_perm(&mk, a.k, BH, a.T, kBF16, fwd::HB) : make_map(&mk, a.k, BH, a.T, a.D, kBF16, fwd::HB);
   if (!make_map(&mq, a.q, BH, a.T, a.D, kBF16, fwd::BM) || !k_ok || !make_map(&mv, a.v, BH, a.T, a.D, kBF16, fwd::HB))
     return cudaErrorInvalidValue;
+  // outputs: O ([B,H,T,D], or [B,T,H,D] through the 4-D view) and the fp32 O, stored by TMA
+  CUtensorMap mo, mo32;
+  const bool o_ok = a.o_bthd ? make_map_bthd(&mo, a.o, a.B, a.H, a.T, a.D, kBF16, fwd::BM)
+                             : make_map(&mo, a.o, BH, a.T, a.D, kBF16, fwd::BM);
+  if (!o_ok) return cudaErrorInvalidValue;
+  if (a.o_f32) {
+    if (!make_map_f32(&mo32, a.o_f32, BH, a.T)) return cudaErrorInvalidValue;
+  } else {
+    mo32 = mo;   // not read: the kernel stores no fp32 O without o_f32
+  }
   auto kern = perm ? fwd::fwd_kernel<kBF16, true> : fwd::fwd_kernel<kBF16, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd::kSmemBytes);
   if (e != cudaSuccess) return e;
   const long long nqt = (a.T + fwd::BM - 1) / fwd::BM;
   return launch_pdl(kern, dim3((unsigned)(BH * nqt)), dim3(fwd::NUM_THREADS), fwd::kSmemBytes, a.stream, mq, mk, mv,
-                    a.v, a.log_gain, a.o, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d,
+                    mo, mo32, a.v, a.log_gain, a.o_f32, a.row_stats, (int)BH, (int)a.H, (int)a.T, a.inv_sqrt_d,
                     a.o_bthd, head_group(BH, nqt));
 }
 

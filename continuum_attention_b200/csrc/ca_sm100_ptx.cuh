@@ -174,6 +174,17 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// 4-D tiled store of a shared-memory box into global memory.  Lane 0.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile(
+      "{\n\t" CA_LANE0_PRED
+      "@l0 cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // order this thread's completed bulk (async-proxy) global writes with its later
 // generic-proxy accesses, and the reverse
 __device__ __forceinline__ void fence_proxy_async_global() {
