@@ -545,12 +545,18 @@ def run_ours(args, world, rank, local):
     launches = 0
     with ClockSampler(local) as clk:
         time.sleep(0.25)   # the sampler's first readings
-        # warm-up right before the timed steps, so that they start on a busy GPU
-        for i in range(args.warmup):
+        # warm-up right before the timed steps, so that they start on a busy GPU: the
+        # W warm-up steps are split around the barrier + synchronize (the last two are
+        # queued after it), so that the K timed steps queue behind running work on
+        # every rank instead of starting on a GPU that the barrier left idle
+        pre = max(args.warmup - 2, 1)
+        for i in range(pre):
             step(i)
         torch.cuda.synchronize()
         _barrier(world)
         torch.cuda.synchronize()
+        for i in range(pre, args.warmup):
+            step(i)
         ev_start.record(stream)
         for i in range(args.steps):
             launches += step(args.warmup + i)
