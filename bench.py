@@ -633,8 +633,10 @@ def run_ours(args, world, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         s_in.wait_event(e0)
+        h0 = time.perf_counter()
         for i in range(e2e_steps):
             e2e_step(i)
+        host_issue_ms = (time.perf_counter() - h0) * 1e3 / e2e_steps
         tail = torch.cuda.Event()
         tail.record(s_out)
         stream.wait_event(tail)
@@ -729,6 +731,7 @@ def run_ours(args, world, rank, local):
                     "host_buffers_numa_local": numa_bound,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps,
                     "copy_floor_ms_per_step": copy_ms,
+                    "host_issue_ms_per_step": host_issue_ms,
                     "frac_of_copy_floor": copy_ms / (e2e_ms / e2e_steps),
                     "copy_floor_note": "the same host<->device copies per step, both directions at once, "
                                        "no compute (same buffers and streams)"},
