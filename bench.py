@@ -703,6 +703,15 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tflops, med, threads, sample = cpu_reference_sample(2, 0)
         cpu = {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        if args.cpu_configs:
+            # the other BASELINE configs the CPU path can time: config 1 and config 3 at
+            # T <= 4096 (longer rows need dense T^2 score tensors of tens of GB)
+            cpu["other_configs"] = {}
+            for name, shp, n, w in (("config1", (2, 4, 256, 32), 5, 1), ("config3_T1024", (1, 16, 1024, 64), 3, 1),
+                                    ("config3_T4096", (1, 16, 4096, 64), 2, 0)):
+                tf, md, _, _ = cpu_reference_sample(n, w, shape=shp)
+                cpu["other_configs"][name] = {"shape": list(shp), "ms_per_step": md * 1e3, "tflops": tf,
+                                              "median_of": n}
 
     clocks = clk.summary()
     # The binding resource of both kernels is the special-function (MUFU) pipe and the
@@ -737,6 +746,10 @@ def run_ours(args, world, rank, local):
                                        "no compute (same buffers and streams)"},
             "roofline": roofline,
             "roofline_mufu": roofline_mufu,
+            # the same steps counted the FlashAttention way (2 forward + 5 backward GEMMs
+            # with the backward's recompute): 7*B*H*T^2*D per step
+            "value_fa_convention": {"value": value * 7.0 / 4.0, "unit": UNIT,
+                                    "flop_per_step": 7.0 * B * H * T * T * D},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": launches,
@@ -756,6 +769,8 @@ def main():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--kernels", choices=["auto", "simt", "tcgen05"], default="auto")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-configs", action="store_true",
+                   help="also time the CPU path at config 1 and config 3 (T = 1024, 4096); about a minute")
     p.add_argument("--no-decoder", action="store_true", help="skip the CA-S decoder tokens/s measurement")
     p.add_argument("--decoder-steps", type=int, default=10)
     p.add_argument("--no-tinylm", action="store_true", help="skip the TinyLM-P small-model measurement")
