@@ -30,9 +30,10 @@ def _run(q, k, v, lg, dy, layout, impl, grad_as_projection):
 @pytest.mark.parametrize("dtype,impl", [(torch.bfloat16, "auto"), (torch.float16, "tcgen05"),
                                         (torch.bfloat16, "simt"), (torch.float32, "auto")])
 @pytest.mark.parametrize("grad_as_projection", [True, False])
-def test_bthd_layout_matches_bhtd(dtype, impl, grad_as_projection):
+@pytest.mark.parametrize("T", [333, 400])   # natural key order; permuted (T % 16 == 0) with a partial tile
+def test_bthd_layout_matches_bhtd(dtype, impl, grad_as_projection, T):
     g = torch.Generator().manual_seed(11)
-    shape = (2, 3, 333, 64)
+    shape = (2, 3, T, 64)
     q, k, v, dy = (torch.randn(shape, generator=g).to(DEV, dtype) for _ in range(4))
     lg = torch.tensor([0.0, 0.3, -0.2], device=DEV)
     y0, g0 = _run(q, k, v, lg, dy, "bhtd", impl, grad_as_projection)
