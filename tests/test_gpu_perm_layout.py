@@ -56,3 +56,14 @@ def test_permuted_and_natural_orders_agree(tmp_path):
     for name, a, b in zip(("dq", "dk", "dv", "dlog_gain"), per[2:], nat[2:]):
         assert cosine(a, b) > 0.99999, name
     assert norm_max_err(per[5], nat[5]) < 1e-3
+
+
+@pytest.mark.parametrize("T", [1, 2, 7, 15, 17, 31, 127, 129])
+def test_tensor_core_kernels_at_tiny_and_odd_lengths(T):
+    # the natural-order kernels (T not a multiple of 16) and one-tile edge cases of the
+    # tensor-core path, against the float64 oracle
+    q, k, v, dy = gen_inputs((2, 3, T, 64), 500 + T, qk_mag=1.5)
+    lg = torch.tensor([0.0, 0.4, -0.4])
+    outs, used = run_op(q, k, v, lg, dy, dtype=torch.bfloat16, impl="tcgen05")
+    ref = oracle(*used[:3], lg, used[3])
+    assert_lowp_parity(outs, ref, tag=f"T={T}")
