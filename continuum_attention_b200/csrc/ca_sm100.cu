@@ -1248,8 +1248,10 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
       issue_grads<kBF16>(sm, st, tmem, t == 0, id_mn, id_dq);
       mma_commit(&sm.bar_mma_done);
       committed = (int)g;
-      // the math warps staged dQ of tile t-1 before arriving on p_ready
-      if (t > 0 && !issue_dq(it, t - 1)) { good = false; break; }
+      // the math warps staged dQ of tile t-1 before arriving on p_ready (in the
+      // deterministic order its turn may still be ahead: that reduce goes out below,
+      // after the ring refill, so that the wait for the turn overlaps it)
+      if (!kDet && t > 0 && !issue_dq(it, t - 1)) { good = false; break; }
       // every math warp is inside this item (it arrived on this tile's p_ready), so
       // the published slot is free: the next item goes out now, and the math warps
       // find it when they finish this one
@@ -1265,6 +1267,7 @@ __device__ void producer(Smem& sm, const CUtensorMap* tq, const CUtensorMap* tk,
         }
         load_kv(nx);
       }
+      if (kDet && t > 0 && !issue_dq(it, t - 1)) { good = false; break; }
       if (t > 0) dq_done();
     }
     if (!good) break;
