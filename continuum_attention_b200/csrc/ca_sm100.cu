@@ -22,7 +22,8 @@
 //   P[c] = B_{kb+c-1} + A_{kb+c} (+ half caps on key 0 and key i),
 // with A_k = M0-M1 and B_k = M1 of segment k (key k-1 -> key k); B of the last
 // key of a half-tile is carried to the next one, and a weight still pending
-// after the last half-tile (query i on its last key) is added in the epilogue.
+// after the last half-tile (query i on its last key) is added in the epilogue,
+// which writes O and the fp32 O through shared-memory staging and TMA stores.
 // Replaces the reference's per-query-tile chain bmm(QK^T) -> scale ->
 // ca_forward_half_kernel -> bmm(W V) (cuda/continuum_attention.py:670-690).
 //
@@ -914,8 +915,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 
 // ---------------------------------------------------------------------------
 // Backward, persistent (one CTA per SM): a work item is one 128-key tile
-// [j0, j0+128) of one head-sequence, looping over the query tiles i0 = j0,
-// j0+128, ...; a CTA takes items heaviest first from a counter (see producer):
+// [j0, j0+128) of one head-sequence, looping over its query tiles from the last
+// one down to the diagonal; a CTA takes items heaviest first from a counter (see
+// producer and decode_item):
 //   warp 16 is the producer (the whole warp runs converged; lane 0 issues):
 //     TMA: K' and V' (keys j0-16 .. j0+143, stationary), Q and dO tiles (2 stages)
 //     S  = Q K'^T   128x160 fp32, TMEM columns [0,160)    (key j0+x at column 16+x)
@@ -925,15 +927,18 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 //     dK += dS^T Q      128x64 fp32, TMEM [448,512)
 //   warps 0-15: thread = (query row 32*(w%4)+lane, key quarter w/4 of 32 keys).
 //     It loads its 34 S and dP values (one halo key each side), forms the 33
-//     segment moments M0..M2, the analytic VJP
-//       dS_j = (R_j + L_{j+1} + cap_j g_j) / Z,   p_j = (B_j + A_{j+1} + cap_j) / Z,
-//     with g = dP - D_i (D_i = dO_i . O_i), and writes p and scale*dS as bf16
-//     into a 128-byte-swizzled shared buffer [2 key halves][128 queries][64 keys].
+//     segment moments M0..M2, the analytic VJP in the form (see bwd_keys8)
+//       p_j = (B_j + A_{j+1} + cap_j) / Z,   dS_j = g_j p_j + H_{j+1} - H_j,
+//     with g = dP - D_i (D_i = dO_i . O_i) and H_k = (g_k - g_{k-1}) (M1 - M2)_k,
+//     and writes p and scale*dS as bf16 into a 128-byte-swizzled shared buffer
+//     [2 key halves][128 queries][64 keys].
 //     The same bytes are the MN-major A operand of dV / dK (M = keys) and the
 //     K-major A operand of dQ (M = queries).  dQ of the previous query tile is
 //     read from TMEM into a swizzled f32 staging tile; the producer adds it to
 //     the global fp32 dQ accumulator with two TMA reduce-adds (32 columns each),
 //     so the adds travel as whole 128-byte rows instead of per-thread atomics.
+//     At an item's end dK and dV leave TMEM through a swizzled staging tile in the
+//     P buffer and two TMA stores.
 // Replaces cuda/continuum_attention.py:713-764 (recompute, dW = dY V^T, the
 // analytic score VJP kernels :192-293/:337-405, and the dV/dQ/dK GEMMs).
 namespace bwd {
