@@ -54,32 +54,36 @@ def _head_subset_ref(used, lg, heads):
     return oracle(sub[0], sub[1], sub[2], lg[heads], sub[3])
 
 
-@pytest.mark.parametrize("impl", ["auto", "simt"])
-def test_config2_bf16_sampled_heads(impl):
-    # [2,16,2048,64] bf16, q,k,v,dy ~ N(0,1), gain 1; oracle on 2 heads x 2 batches
+@pytest.mark.parametrize("impl,dtype", [("auto", torch.bfloat16), ("simt", torch.bfloat16),
+                                        ("auto", torch.float16)])
+def test_config2_sampled_heads(impl, dtype):
+    # [2,16,2048,64] bf16, q,k,v,dy ~ N(0,1), gain 1; oracle on 2 heads x 2 batches.
+    # The fp16 case pins the tensor-core forward's single-fp16 P at full length.
     q, k, v, dy = gen_inputs((2, 16, 2048, 64), 2)
     lg = torch.zeros(16)
-    outs, used = run_op(q, k, v, lg, dy, dtype=torch.bfloat16, impl=impl)
+    outs, used = run_op(q, k, v, lg, dy, dtype=dtype, impl=impl)
     heads = [0, 11]
     y, rdq, rdk, rdv, rdg = _head_subset_ref(used, lg, heads)
     o, o32, dq, dk, dv, dg = outs
     sub = lambda t: t[:, heads]
     assert_lowp_parity((sub(o), sub(o32), sub(dq), sub(dk), sub(dv), dg[heads]),
-                       (y, rdq, rdk, rdv, rdg), tag=f"config2[{impl}]")
+                       (y, rdq, rdk, rdv, rdg), tag=f"config2[{impl},{dtype}]", lowp_dtype=dtype)
 
 
+@pytest.mark.parametrize("dtype", LOWP)
 @pytest.mark.parametrize("T", [1024, 4096])
-def test_config3_stress_sampled_heads(T):
-    # [1,16,T,64] bf16, score std ~4, 10% adjacent keys duplicated (delta = 0)
+def test_config3_stress_sampled_heads(T, dtype):
+    # [1,16,T,64] bf16, score std ~4, 10% adjacent keys duplicated (delta = 0);
+    # also in fp16 (single-fp16 P in the tensor-core forward)
     q, k, v, dy = gen_inputs((1, 16, T, 64), 3000 + T, qk_mag=2.0, dup_frac=0.1)
     lg = torch.zeros(16)
-    outs, used = run_op(q, k, v, lg, dy, dtype=torch.bfloat16)
+    outs, used = run_op(q, k, v, lg, dy, dtype=dtype)
     heads = [3]
     y, rdq, rdk, rdv, rdg = _head_subset_ref(used, lg, heads)
     o, o32, dq, dk, dv, dg = outs
     sub = lambda t: t[:, heads]
     assert_lowp_parity((sub(o), sub(o32), sub(dq), sub(dk), sub(dv), dg[heads]),
-                       (y, rdq, rdk, rdv, rdg), tag=f"config3 T={T}")
+                       (y, rdq, rdk, rdv, rdg), tag=f"config3 T={T} {dtype}", lowp_dtype=dtype)
 
 
 def test_fp32_and_lowp_paths_agree_on_larger_shape():
